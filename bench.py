@@ -1,0 +1,410 @@
+"""Benchmark: paged-attention decode, achieved HBM GB/s on cold pools.
+
+Workload: GPT-2 geometry decode step, 12 layers,
+H = HKV = 12, D = 64, block_size 16, batch 64, context 2048, fp16 KV pool,
+synthetic N(0, 1) data.  A step = one decode token for every sequence through
+all 12 layers (12 ``paged_attention_v3`` calls, one per layer's pool view).
+Cold pools: 4 disjoint block regions of the pool, rotated step by step, so
+each step reads 4.84 GB and the rotation spans 19.3 GB (L2 is 126 MB): every
+KV byte comes from HBM.
+
+value      kernel-only throughput: algorithmic bytes (KV once per KV head + q +
+           out + block-table entries) / device time of the K timed steps,
+           inputs resident in HBM, CUDA events, max over ranks.
+e2e        the same metric through the public API (pa_b200.ops, the torch
+           shim over the C ABI) with q in pinned HOST memory: each step copies
+           q (and the step's block table) host->device and the outputs
+           device->host inside the timed region.
+roofline   the decode kernel: bytes per launch / launch time, against the
+           measured copy bandwidth of this pool's B200s.
+N > 1      one process per GPU (torchrun); each rank runs the same per-GPU
+           workload (weak scaling, batch sharding: no collective on the data
+           path); value = all ranks' bytes / slowest rank's time.
+
+--impl reference times the reference's scalar FP32 CPU decode (the oracle's
+restatement of gb10-attn rocm/hip/paged_attn_v1_hip.cpp:104-141; the HIP file
+itself does not build here) on the host cores, on a bounded sample of the
+same workload, and prints the same metric.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+import numpy as np
+
+REPO = Path(__file__).resolve().parent
+sys.path.insert(0, str(REPO / "gb10-attn_b200"))
+sys.path.insert(0, str(REPO))
+
+METRIC = "decode achieved HBM GB/s (% of B200 peak), cold pools; tokens/s at 1/2/4/8 GPUs"
+
+# configs[1] geometry
+L, H, HKV, D, BS, B, CTX = 12, 12, 12, 64, 16, 64, 2048
+REGIONS = 4
+
+
+def _env_rank():
+    return (int(os.environ.get("RANK", 0)), int(os.environ.get("LOCAL_RANK", 0)),
+            int(os.environ.get("WORLD_SIZE", 1)))
+
+
+def _peaks() -> dict:
+    p = REPO / "MEASURED_PEAKS.json"
+    if p.exists():
+        try:
+            d = json.loads(p.read_text())
+            return {"hbm_gbs": float(d["hbm_gbs"]), "src": "measured"}
+        except (OSError, ValueError, KeyError):
+            pass
+    return {"hbm_gbs": 6650.0, "src": "fallback"}
+
+
+def _profile_traffic(kernel_key: str) -> float | None:
+    """DRAM bytes per launch of the decode kernel from the committed ncu
+    summary (a line 'traffic_bytes_per_launch: N' in profiles/*.md)."""
+    for p in sorted((REPO / "profiles").glob(f"{kernel_key}*.md")):
+        for line in p.read_text().splitlines():
+            if line.strip().startswith("traffic_bytes_per_launch:"):
+                try:
+                    return float(line.split(":", 1)[1].strip().split()[0])
+                except ValueError:
+                    return None
+    return None
+
+
+class ClockSampler:
+    """nvidia-smi clock / throttle samples during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.idx = gpu_index
+        self.proc = None
+        self.lines: list[str] = []
+        self.t = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-i", str(self.idx), "-lms", "100"], stdout=subprocess.PIPE,
+                stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+            time.sleep(0.3)
+        except (OSError, FileNotFoundError):
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *exc):
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+            if self.t:
+                self.t.join(timeout=2)
+
+    def summary(self) -> dict:
+        sm, mx, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in self.lines:
+            f = [x.strip() for x in line.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx.append(float(f[2]))
+            except ValueError:
+                continue
+            for n, val in zip(names, f[5:9]):
+                if val.lower() == "active":
+                    reasons.add(n)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(mx),
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# ---------------------------------------------------------------------------
+# the B200 arm
+# ---------------------------------------------------------------------------
+
+def run_b200(args) -> None:
+    import torch
+    import torch.distributed as dist
+
+    from pa_b200 import harness, ops
+
+    rank, local, world = _env_rank()
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    if world > 1:
+        import datetime
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=dev)
+
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(1234 + rank)
+    nb = B * (CTX // BS) * REGIONS  # 32768 blocks per layer pool
+    # one [2, NB, BS, HKV, D] tensor per layer (the reference's per-layer pool)
+    pools = []
+    for _ in range(L):
+        t = torch.empty((2, nb, BS, HKV, D), dtype=torch.float16, device=dev)
+        t.normal_(generator=gen)
+        pools.append(t)
+    q_dev = torch.randn((L, B, H, D), generator=gen, device=dev, dtype=torch.float32)
+    ctx_np = np.full(B, CTX, np.int32)
+    tables = harness.cold_regions([CTX // BS] * B, REGIONS, nb, seed=rank)
+    bt_dev = [torch.from_numpy(t).to(dev) for t in tables]
+    ctx_dev = torch.from_numpy(ctx_np).to(dev)
+    scale = D ** -0.5
+    outs = torch.empty((L, B, H, D), dtype=torch.float32, device=dev)
+    stream = torch.cuda.current_stream()
+
+    bytes_per_call = harness.decode_bytes(ctx_np, H, HKV, D, 2, BS)
+    bytes_per_step = L * bytes_per_call
+
+    def step(i: int):
+        bt = bt_dev[i % REGIONS]
+        for layer in range(L):
+            outs[layer] = ops.paged_attention_v3(q_dev[layer], pools[layer][0], pools[layer][1],
+                                                 bt, ctx_dev, scale, 0)
+
+    # correctness gate (the reference's bench checks every path before timing,
+    # docs/REPORT.md:41-43): layer 0 against a dense torch fp32 reference
+    bt0 = tables[0]
+    kf = pools[0][0].float()
+    vf = pools[0][1].float()
+    ref_err = 0.0
+    for b in range(0, B, 16):
+        blocks = torch.from_numpy(bt0[b, :CTX // BS].astype(np.int64)).to(dev)
+        kk = kf[blocks].reshape(CTX, HKV, D)
+        vv = vf[blocks].reshape(CTX, HKV, D)
+        s = torch.einsum("hd,thd->ht", q_dev[0, b], kk) * scale
+        want = torch.einsum("ht,thd->hd", torch.softmax(s, -1), vv)
+        got = ops.paged_attention_v3(q_dev[0, b:b + 1], pools[0][0], pools[0][1],
+                                     bt_dev[0][b:b + 1], ctx_dev[b:b + 1], scale, 0)[0]
+        ref_err = max(ref_err, float((got - want).abs().max()))
+    del kf, vf
+    torch.cuda.empty_cache()
+    if ref_err > 2e-3:
+        raise SystemExit(f"correctness gate failed: max-abs {ref_err}")
+
+    for i in range(args.warmup):
+        step(i)
+    torch.cuda.synchronize()
+
+    # --- kernel-only timed region -----------------------------------------
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clocks:
+        ev0.record(stream)
+        for i in range(args.steps):
+            step(i)
+        ev1.record(stream)
+        torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    t_ms = ev0.elapsed_time(ev1)
+
+    # --- per-launch decode time (same stream, events around each call) -----
+    n_launch = min(L * 4, L * args.steps)
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+           for _ in range(n_launch)]
+    torch.cuda.synchronize()
+    for j, (a, b_) in enumerate(evs):
+        layer = j % L
+        a.record(stream)
+        outs[layer] = ops.paged_attention_v3(q_dev[layer], pools[layer][0], pools[layer][1],
+                                             bt_dev[(j // L) % REGIONS], ctx_dev, scale, 0)
+        b_.record(stream)
+    torch.cuda.synchronize()
+    launch_ms = statistics.mean(a.elapsed_time(b_) for a, b_ in evs)
+
+    # --- end to end through the public API with host buffers ---------------
+    q_host = torch.empty((L, B, H, D), dtype=torch.float32).pin_memory()
+    q_host.copy_(q_dev.cpu())
+    bt_host = [torch.from_numpy(t).pin_memory() for t in tables]
+    ctx_host = torch.from_numpy(ctx_np).pin_memory()
+    out_host = torch.empty((L, B, H, D), dtype=torch.float32).pin_memory()
+
+    def e2e_step(i: int):
+        qd = q_host.to(dev, non_blocking=True)
+        btd = bt_host[i % REGIONS].to(dev, non_blocking=True)
+        cd = ctx_host.to(dev, non_blocking=True)
+        for layer in range(L):
+            o = ops.paged_attention_v3(qd[layer], pools[layer][0], pools[layer][1], btd, cd,
+                                       scale, 0)
+            out_host[layer].copy_(o, non_blocking=True)
+
+    for i in range(max(2, args.warmup)):
+        e2e_step(i)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for i in range(args.steps):
+        e2e_step(i)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    e2e_ms = e0.elapsed_time(e1)
+    h2d = q_host.numel() * 4 + bt_host[0].numel() * 4 + ctx_host.numel() * 4
+    d2h = out_host.numel() * 4
+
+    # max over ranks
+    times = torch.tensor([t_ms, e2e_ms, launch_ms], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(times, op=dist.ReduceOp.MAX)
+    t_ms, e2e_ms, launch_ms = (float(x) for x in times.cpu())
+
+    total_bytes = bytes_per_step * args.steps * world
+    value = total_bytes / (t_ms * 1e-3) / 1e9
+    e2e_val = total_bytes / (e2e_ms * 1e-3) / 1e9
+    peaks = _peaks()
+    achieved = bytes_per_call / (launch_ms * 1e-3) / 1e9
+    traffic = _profile_traffic("decode_kernel")
+    clk = clocks.summary()
+
+    line = {
+        "metric": METRIC, "value": round(value, 1), "unit": "GB/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(t_ms / args.steps, 4), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f16",
+        "data": "synthetic N(0,1) KV pool and q, seeded",
+        "config": {"workload": "configs[1]: gpt2 paged decode, 12 layers, B=64/GPU, ctx=2048, "
+                               "H=HKV=12, D=64, block_size=16, fp16 KV, fp32 q/out",
+                   "global_batch": B * world, "seq_len": CTX, "layers": L,
+                   "parallelism": f"batch-sharded x{world} (no collective)",
+                   "cold": f"{REGIONS} disjoint block regions rotated per step; inputs larger "
+                           f"than L2 ({bytes_per_step / 1e9:.2f} GB/step, "
+                           f"{REGIONS * bytes_per_step / 1e9:.1f} GB rotation)",
+                   "tokens_per_s": round(B * world * args.steps / (t_ms * 1e-3), 1),
+                   "pct_of_measured_hbm_peak": round(100 * value / world / peaks["hbm_gbs"], 1),
+                   "pct_of_spec_8TBs": round(100 * value / world / 8000.0, 1),
+                   "correctness_gate_max_abs": ref_err},
+        "e2e": {"value": round(e2e_val, 1), "unit": "GB/s", "h2d_bytes_per_step": h2d,
+                "d2h_bytes_per_step": d2h,
+                "tokens_per_s": round(B * world * args.steps / (e2e_ms * 1e-3), 1)},
+        "gpu_launches": 2 * L * args.steps,
+        "roofline": {"bound": "hbm", "achieved": round(achieved, 1),
+                     "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                     "frac": round(achieved / peaks["hbm_gbs"], 4),
+                     "traffic": traffic, "peak_source": peaks["src"],
+                     "kernel": "pa::decode::decode_kernel<__half,64,1> (+ plan_kernel, PDL)",
+                     "bytes_per_launch": bytes_per_call,
+                     "launch_us": round(launch_ms * 1e3, 2)},
+        "clocks": clk,
+    }
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        line["cpu_baseline"] = cpu_baseline(args.cpu_seconds)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+
+
+# ---------------------------------------------------------------------------
+# the CPU reference arm / baseline
+# ---------------------------------------------------------------------------
+
+def cpu_sample(seconds: float, threads: int):
+    """Times the oracle restatement of the reference's scalar FP32 CPU decode
+    on layer calls of the config-2 workload (fp16 values upcast to fp32, as
+    the reference's CPU path computes in fp32) until `seconds` have passed.
+    Returns (GB/s by the same algorithmic-bytes model, calls, sample text)."""
+    from oracle import oracle as orc
+    from pa_b200 import harness
+
+    q, k, v, bt, ctx = orc.make_decode_case(7, B, H, HKV, D, BS, CTX)
+    k = orc.round_to(k, "float16")
+    v = orc.round_to(v, "float16")
+    orc.decode(q[:1], k, v, bt[:1], ctx[:1], D ** -0.5, threads=1)  # warm
+    per_call = harness.decode_bytes(ctx, H, HKV, D, 2, BS)
+    n, t0 = 0, time.perf_counter()
+    while True:
+        orc.decode(q, k, v, bt, ctx, D ** -0.5, threads=threads)
+        n += 1
+        el = time.perf_counter() - t0
+        if el >= seconds:
+            break
+    gbs = n * per_call / el / 1e9
+    sample = (f"{n} full layer calls (B=64, ctx=2048, H=12, D=64) of the config-2 workload, "
+              f"{el:.1f} s, {threads} threads")
+    return gbs, n, sample
+
+
+def cpu_baseline(seconds: float) -> dict:
+    threads = os.cpu_count() or 1
+    gbs, _, sample = cpu_sample(seconds, threads)
+    return {"value": round(gbs, 3), "unit": "GB/s", "cores": threads, "kind": "port",
+            "sample": sample}
+
+
+def run_reference(args) -> None:
+    rank, _, world = _env_rank()
+    if rank != 0:
+        return
+    threads = os.cpu_count() or 1
+    per_step = []
+    for _ in range(args.warmup):
+        cpu_sample(0.0, threads)
+    for _ in range(args.steps):
+        gbs, _, sample = cpu_sample(args.ref_step_seconds, threads)
+        per_step.append(gbs)
+    value = statistics.mean(per_step)
+    line = {
+        "impl": "reference", "metric": METRIC, "value": round(value, 3), "unit": "GB/s",
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic N(0,1), seeded",
+        "config": {"workload": "configs[1] decode layer calls, B=64, ctx=2048, H=HKV=12, "
+                               "D=64, fp16 values computed in fp32 on the host",
+                   "parallelism": f"{threads} host threads, rank 0 only"},
+        "cpu_baseline": {"value": round(value, 3), "unit": "GB/s", "cores": threads,
+                         "kind": "port", "sample": sample},
+        "e2e": {"value": round(value, 3), "unit": "GB/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser(description=__doc__.split("\n")[0])
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
+    ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    ap.add_argument("--ref-step-seconds", type=float, default=3.0)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_b200(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,558 @@
+// decode_impl.cuh -- split-KV paged decode for sm_100a.
+//
+// Replaces paged_attention_split_kernel + merge_splits_kernel of
+// gb10-attn kernels/paged_attn_v3.cu:33-166 (and the v1/v2 decode kernels,
+// which compute the same function).  Same math: online softmax per piece of
+// context, un-normalised partials, log-sum-exp merge (:113-122, :139-165).
+// Different machine mapping:
+//
+//   * Work unit = a tile of kTT = 16 consecutive tokens of one sequence for a
+//     group of G kv heads ("g-chunk").  The NGC * sum_b ceil(ctx_b / 16) tiles
+//     are split into N equal contiguous ranges, one per CTA (N = SMs x
+//     resident CTAs for automatic splitting), so every SM streams the same
+//     number of bytes whatever the context lengths (stream-K style).
+//   * One producer warp per CTA issues 1-D bulk (TMA) copies of the token
+//     rows [G kv heads x D] of K and V straight from the pages into a ring of
+//     shared-memory stages guarded by mbarriers.  A stage is 16 tokens; a row
+//     is G*D*sizeof(T) contiguous bytes of a page.  No multicast.
+//   * Each consumer warp owns one "slot": one kv head of the g-chunk and QC of
+//     the query heads that share it (GQA), so every KV byte is read from HBM
+//     once and from shared memory once per slot.  Inside a warp, R lanes
+//     hold one token row (lane owns EPL elements, 16-byte shared loads) and
+//     the 32/R row groups take different tokens, each keeping its own online
+//     softmax state (m, l, acc) in registers; the row groups are merged with
+//     shuffles once per segment, not per token.
+//   * A sequence whose tiles span several CTAs is merged by the CTA that
+//     finishes its piece last (per-(sequence, slot) arrival counter), so no
+//     second kernel and no extra partial round trip for unsplit sequences.
+//
+// Scores are kept in the log2 domain (q pre-scaled by scale*log2(e)) so each
+// exponential is one ex2.approx; the reference's __expf is the same
+// instruction after a multiply.
+#pragma once
+
+#include "common.cuh"
+
+namespace pa {
+namespace decode {
+
+constexpr int kTT = 16;            // tokens per pipeline stage
+constexpr float kNegBig = -3.0e38f;  // the reference's "minus infinity" (paged_attn_v3.cu:20)
+
+struct Params {
+  float* out;                    // [B, H, D]
+  float* lse;                    // [B, H] or null
+  const float* q;                // [B, H, D]
+  const char* k_cache;           // [NB, BS, HKV, D] bytes
+  const char* v_cache;
+  const int32_t* block_tables;   // [B, MB]
+  const int32_t* context_lens;   // [B]
+  int32_t* dev_status;           // nullable
+  const int32_t* tile_off;       // [B + 1] tiles before sequence b (per g-chunk)
+  const int32_t* cta_seq;        // [N] sequence holding each CTA's first tile
+  int32_t* counters;             // [NGC * B * NS] merge arrival counters
+  int32_t* abort_flag;           // set when any pipeline wait times out
+  float* partials;               // [N * 2 * NS * QC * (D + 2)]
+  int64_t B, H, HKV, NB, MB, BS;
+  // Query rows per block-table row: 1 for decode.  For causal prefill row
+  // b' = b * qlen + s is query s of sequence b; it reads block_tables[b] and
+  // sees keys [0, context_lens[b] - qlen + s] (paged_attn_prefill.cu:62-65).
+  int64_t qlen;
+  int32_t G, QPK, NS, NGC, N, nstage;
+  float qscale;                  // scale * log2(e)
+  uint32_t row_bytes;            // G * D * sizeof(T)
+  int64_t tok_stride;            // HKV * D * sizeof(T): one token row of a page
+  int64_t blk_stride;            // BS * tok_stride: one page
+};
+
+struct __align__(16) StageHeader {
+  int32_t b, gc, tok0, nvalid;
+  int32_t flags, pad0, pad1, pad2;
+  int64_t gt, seq_t0, seq_t1, pad3;
+};
+constexpr int kFirst = 1, kLast = 2, kEnd = 4;
+
+// Lane geometry for element type T and head_dim D.
+template <typename T, int D>
+struct Geo {
+  static constexpr int VEC = Chunk<T>::N;                 // elements per 16 B
+  static constexpr int CH = D / VEC;                      // 16 B chunks per row
+  static constexpr int R = CH <= 8 ? CH : (CH / 2 > 32 ? 32 : CH / 2);  // lanes per row
+  static constexpr int NCH = CH / R;                      // chunks per lane
+  static constexpr int EPL = NCH * VEC;                   // elements per lane
+  static constexpr int NRG = 32 / R;                      // row groups per warp
+  static constexpr int TPR = kTT / NRG;                   // tokens per row group per stage
+  static_assert(D % VEC == 0 && CH % R == 0 && 32 % R == 0 && NRG <= kTT, "geometry");
+};
+
+// CTA shape of a (T, D, QC) instantiation.
+//  * Light state (q and acc, 2 * QC * EPL floats, <= 16): up to 16 consumer
+//    warps 0..NS-1 plus the producer warp NS; (NS + 1) * 32 threads.
+//  * Heavier state (GQA groups, or head_dim >= 128): warp-specialised
+//    warpgroups.  Warpgroup 0 is the producer (warp 0 issues copies, warps 1-3
+//    retire) and gives registers back with setmaxnreg.dec to kProdRegs;
+//    warpgroups 1-2 are 8 consumer warps that raise their budget to
+//    kConsRegs.  Launched with 384 threads x 168 registers (12 warps, 3 per
+//    SM sub-partition) = 64512; after the split 128 x 48 + 256 x 224 = 63488,
+//    inside the launch total as setmaxnreg.inc requires.
+template <typename T, int D, int QC>
+struct Limits {
+  static constexpr bool WS =
+      (QC * Geo<T, D>::EPL >= 16) || (sizeof(T) >= 4 && QC * Geo<T, D>::EPL >= 8);
+  static constexpr int MAXW = WS ? 8 : 16;
+  static constexpr int THREADS = WS ? 384 : (MAXW + 1) * 32;
+};
+constexpr int kProdRegs = 48;
+constexpr int kConsRegs = 224;
+static_assert(128 * kProdRegs + 256 * kConsRegs <= 384 * 168, "register split exceeds launch");
+
+__device__ __forceinline__ int64_t cta_lo(int64_t c, int64_t T_all, int64_t N) {
+  return c * T_all / N;
+}
+// CTA whose range holds global tile t: the largest c with cta_lo(c) <= t.
+__device__ __forceinline__ int64_t cta_of(int64_t t, int64_t T_all, int64_t N) {
+  return ((t + 1) * N - 1) / T_all;
+}
+
+template <typename T, int D, int QC>
+__global__ void __launch_bounds__(Limits<T, D, QC>::THREADS, 1)
+    decode_kernel(const __grid_constant__ Params p) {
+  using G_ = Geo<T, D>;
+  constexpr int VEC = G_::VEC, R = G_::R, NCH = G_::NCH, EPL = G_::EPL;
+  constexpr int NRG = G_::NRG, TPR = G_::TPR;
+
+  extern __shared__ __align__(128) unsigned char smem[];
+  const int nstage = p.nstage;
+  const uint32_t stage_bytes = 2u * kTT * p.row_bytes;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + (size_t)nstage * stage_bytes);
+  uint64_t* empty = full + nstage;
+  StageHeader* hdr = reinterpret_cast<StageHeader*>(empty + nstage);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int NS = p.NS;
+  constexpr bool WS = Limits<T, D, QC>::WS;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < nstage; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], NS);
+    }
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  __syncthreads();
+  // Everything above overlaps the plan kernel; its tables are read below.
+  pdl_wait();
+
+  const int64_t Tpg = p.tile_off[p.B];  // tiles per g-chunk
+  const int64_t T_all = Tpg * p.NGC;
+  const int64_t cta = blockIdx.x;
+  const int64_t lo = cta_lo(cta, T_all, p.N), hi = cta_lo(cta + 1, T_all, p.N);
+
+  if constexpr (WS) {
+    if (warp < 4) {
+      asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kProdRegs));
+      if (warp != 0) return;
+    } else {
+      asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kConsRegs));
+      if (warp - 4 >= NS) return;
+    }
+  }
+  const bool is_producer = WS ? (warp == 0) : (warp == NS);
+
+  if (is_producer) {
+    // ------------------------------------------------------------------ producer
+    int stage = 0;
+    uint32_t phase = 0;
+    bool ok = true;
+    if (lo < hi) {
+      int64_t gt = lo;
+      int gc = (int)(lo / Tpg);
+      int64_t r = lo - (int64_t)gc * Tpg;
+      int b = p.cta_seq[cta];
+      int64_t s0 = p.tile_off[b], s1 = p.tile_off[b + 1];
+      const int64_t max_ctx = p.MB * p.BS;
+      auto seq_len = [&](int bb) -> int64_t {
+        const int64_t sq = bb / p.qlen;
+        int64_t n = (int64_t)p.context_lens[sq] - p.qlen + (bb - sq * p.qlen) + 1;
+        if (n > max_ctx) n = max_ctx;
+        return n < 0 ? 0 : n;
+      };
+      int64_t n_tok = seq_len(b);
+      const int32_t* bt = p.block_tables + (int64_t)(b / p.qlen) * p.MB;
+      auto bt_load = [&](int64_t idx) -> int32_t {
+        return (idx >= 0 && idx < p.MB) ? __ldg(bt + idx) : 0;
+      };
+      int64_t win_base = -1;
+      int32_t win_cur = 0, win_next = 0;
+      const int64_t gbytes = (int64_t)p.G * D * (int64_t)sizeof(T);
+      const uint32_t qbytes = (uint32_t)(p.G * p.QPK * D * 4);
+
+      while (gt < hi) {
+        const int64_t t_in_seq = r - s0;
+        const int64_t tok0 = t_in_seq * kTT;
+        const int nvalid = (int)(n_tok - tok0 < kTT ? n_tok - tok0 : kTT);
+        // block-table window: lane l holds bt[win_base + l] (cur) and
+        // bt[win_base + 32 + l] (next); `next` is loaded a window ahead.
+        const int64_t pg_lo = tok0 / p.BS;
+        if (win_base < 0 || pg_lo >= win_base + 32) {
+          if (win_base >= 0 && pg_lo < win_base + 64) {
+            win_base += 32;
+            win_cur = win_next;
+          } else {
+            win_base = pg_lo;
+            win_cur = bt_load(win_base + lane);
+          }
+          win_next = bt_load(win_base + 32 + lane);
+        }
+        if (!mbar_wait(&empty[stage], phase ^ 1, p.abort_flag)) { ok = false; break; }
+
+        const int row = lane & 15, kv = lane >> 4;
+        const int64_t tok = tok0 + row;
+        const int64_t pg = tok / p.BS;
+        const int idx = (int)(pg - win_base);
+        const int32_t a = __shfl_sync(0xffffffffu, win_cur, idx & 31);
+        const int32_t c = __shfl_sync(0xffffffffu, win_next, idx & 31);
+        int64_t blk = idx < 32 ? a : c;
+        bool bad = false;
+        if (row < nvalid && (blk < 0 || blk >= p.NB)) { bad = true; blk = 0; }
+        if (__any_sync(0xffffffffu, bad) && lane == 0) report(p.dev_status, PA_DEVERR_BLOCK_ID);
+
+        if (lane == 0) {
+          StageHeader& h = hdr[stage];
+          const bool first = (gt == lo) || (t_in_seq == 0);
+          h.b = b;
+          h.gc = gc;
+          h.tok0 = (int32_t)tok0;
+          h.nvalid = nvalid;
+          h.flags = (first ? kFirst : 0) | ((gt + 1 == hi || r + 1 == s1) ? kLast : 0);
+          h.gt = gt;
+          h.seq_t0 = (int64_t)gc * Tpg + s0;
+          h.seq_t1 = (int64_t)gc * Tpg + s1;
+          if (first)
+            prefetch_l2(p.q + ((int64_t)b * p.H + (int64_t)gc * p.G * p.QPK) * D, qbytes);
+          mbar_arrive_expect_tx(&full[stage], (uint32_t)nvalid * 2u * p.row_bytes);
+        }
+        __syncwarp();
+        if (row < nvalid) {
+          const int64_t off = tok - pg * p.BS;
+          const char* src = (kv ? p.v_cache : p.k_cache) + blk * p.blk_stride +
+                            off * p.tok_stride + (int64_t)gc * gbytes;
+          unsigned char* dst = smem + (size_t)stage * stage_bytes +
+                               (size_t)(kv * kTT + row) * p.row_bytes;
+          bulk_g2s(dst, src, p.row_bytes, &full[stage]);
+        }
+
+        ++gt;
+        ++r;
+        if (++stage == nstage) { stage = 0; phase ^= 1; }
+        if (gt < hi && r == s1) {
+          if (r == Tpg) { ++gc; r = 0; b = 0; }
+          else ++b;
+          while (p.tile_off[b + 1] == p.tile_off[b]) ++b;  // skip empty sequences
+          s0 = p.tile_off[b];
+          s1 = p.tile_off[b + 1];
+          n_tok = seq_len(b);
+          bt = p.block_tables + (int64_t)(b / p.qlen) * p.MB;
+          win_base = -1;
+        }
+      }
+    }
+    if (ok && mbar_wait(&empty[stage], phase ^ 1, p.abort_flag)) {
+      if (lane == 0) {
+        hdr[stage].flags = kEnd;
+        mbar_arrive(&full[stage]);
+      }
+    } else if (lane == 0) {
+      // The consumers then give up on their own bounded full-barrier wait.
+      // Copies already issued complete within microseconds, long before any
+      // 1 s wait expires, so no copy is in flight when the CTA retires.
+      report(p.dev_status, PA_DEVERR_TIMEOUT);
+    }
+    return;
+  }
+
+  // -------------------------------------------------------------------- consumers
+  const int slot = WS ? warp - 4 : warp;
+  const int slots_per_g = p.QPK / QC;
+  const int g_local = slot / slots_per_g;
+  const int hq0 = (slot % slots_per_g) * QC;
+  const int rg = lane / R, li = lane % R;
+
+  float qf[QC][EPL];
+  float acc[QC][EPL];
+  float m[QC], l[QC];
+#pragma unroll
+  for (int j = 0; j < QC; ++j) {
+    m[j] = kNegBig;
+    l[j] = 0.f;
+#pragma unroll
+    for (int e = 0; e < EPL; ++e) { acc[j][e] = 0.f; qf[j][e] = 0.f; }
+  }
+
+  int stage = 0;
+  uint32_t phase = 0;
+  int seg_count = 0;
+  int64_t seg_gt0 = 0;
+  int b = 0, gc = 0;
+  int64_t head0 = 0;
+
+  while (true) {
+    if (!mbar_wait(&full[stage], phase, p.abort_flag)) {
+      if (lane == 0) report(p.dev_status, PA_DEVERR_TIMEOUT);
+      break;
+    }
+    const StageHeader h = hdr[stage];
+    if (h.flags & kEnd) break;
+
+    if (h.flags & kFirst) {
+      b = h.b;
+      gc = h.gc;
+      seg_gt0 = h.gt;
+      head0 = ((int64_t)gc * p.G + g_local) * p.QPK + hq0;
+      const float* qp = p.q + ((int64_t)b * p.H + head0) * D;
+#pragma unroll
+      for (int j = 0; j < QC; ++j) {
+#pragma unroll
+        for (int c = 0; c < NCH; ++c) {
+          const float* src = qp + (int64_t)j * D + (c * R + li) * VEC;
+#pragma unroll
+          for (int v = 0; v < VEC; v += 2) {
+            const float2 x = *reinterpret_cast<const float2*>(src + v);
+            qf[j][c * VEC + v] = x.x * p.qscale;
+            qf[j][c * VEC + v + 1] = x.y * p.qscale;
+          }
+        }
+        m[j] = kNegBig;
+        l[j] = 0.f;
+#pragma unroll
+        for (int e = 0; e < EPL; ++e) acc[j][e] = 0.f;
+      }
+    }
+
+    const unsigned char* kbase =
+        smem + (size_t)stage * stage_bytes + (size_t)g_local * D * sizeof(T);
+    const unsigned char* vbase = kbase + (size_t)kTT * p.row_bytes;
+    const int nvalid = h.nvalid;
+
+    // scores of this row group's tokens for the QC heads
+    float s[TPR][QC];
+#pragma unroll
+    for (int i = 0; i < TPR; ++i) {
+      const int t = rg + i * NRG;
+#pragma unroll
+      for (int j = 0; j < QC; ++j) s[i][j] = 0.f;
+      const unsigned char* kr = kbase + (size_t)t * p.row_bytes;
+#pragma unroll
+      for (int c = 0; c < NCH; ++c) {
+        float kf[VEC];
+        Chunk<T>::cvt(lds128(kr + (size_t)(c * R + li) * 16), kf);
+#pragma unroll
+        for (int j = 0; j < QC; ++j)
+#pragma unroll
+          for (int v = 0; v < VEC; ++v) s[i][j] = fmaf(qf[j][c * VEC + v], kf[v], s[i][j]);
+      }
+    }
+#pragma unroll
+    for (int off = R / 2; off >= 1; off >>= 1)
+#pragma unroll
+      for (int i = 0; i < TPR; ++i)
+#pragma unroll
+        for (int j = 0; j < QC; ++j) s[i][j] += __shfl_xor_sync(0xffffffffu, s[i][j], off);
+
+    // online softmax update (one rescale per stage)
+#pragma unroll
+    for (int j = 0; j < QC; ++j) {
+      float mx = m[j];
+#pragma unroll
+      for (int i = 0; i < TPR; ++i)
+        if (rg + i * NRG < nvalid) mx = fmaxf(mx, s[i][j]);
+      const float corr = fast_exp2(m[j] - mx);
+      m[j] = mx;
+      float lsum = l[j] * corr;
+#pragma unroll
+      for (int e = 0; e < EPL; ++e) acc[j][e] *= corr;
+#pragma unroll
+      for (int i = 0; i < TPR; ++i) {
+        const float pv = (rg + i * NRG < nvalid) ? fast_exp2(s[i][j] - mx) : 0.f;
+        s[i][j] = pv;
+        lsum += pv;
+      }
+      l[j] = lsum;
+    }
+#pragma unroll
+    for (int i = 0; i < TPR; ++i) {
+      const int t = rg + i * NRG;
+      if (t < nvalid) {
+        const unsigned char* vr = vbase + (size_t)t * p.row_bytes;
+#pragma unroll
+        for (int c = 0; c < NCH; ++c) {
+          float vf[VEC];
+          Chunk<T>::cvt(lds128(vr + (size_t)(c * R + li) * 16), vf);
+#pragma unroll
+          for (int j = 0; j < QC; ++j)
+#pragma unroll
+            for (int v = 0; v < VEC; ++v)
+              acc[j][c * VEC + v] = fmaf(s[i][j], vf[v], acc[j][c * VEC + v]);
+        }
+      }
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&empty[stage]);
+    if (++stage == nstage) { stage = 0; phase ^= 1; }
+
+    if (!(h.flags & kLast)) continue;
+
+    // ---------------------------------------------------------- segment end
+    // merge the row groups of this warp
+#pragma unroll
+    for (int off = R; off < 32; off <<= 1) {
+#pragma unroll
+      for (int j = 0; j < QC; ++j) {
+        const float mo = __shfl_xor_sync(0xffffffffu, m[j], off);
+        const float lo_ = __shfl_xor_sync(0xffffffffu, l[j], off);
+        const float mn = fmaxf(m[j], mo);
+        const float wa = fast_exp2(m[j] - mn), wb = fast_exp2(mo - mn);
+        l[j] = l[j] * wa + lo_ * wb;
+#pragma unroll
+        for (int e = 0; e < EPL; ++e) {
+          const float ao = __shfl_xor_sync(0xffffffffu, acc[j][e], off);
+          acc[j][e] = acc[j][e] * wa + ao * wb;
+        }
+        m[j] = mn;
+      }
+    }
+
+    const bool split = (h.seq_t0 < seg_gt0) || (h.seq_t1 > h.gt + 1);
+    if (!split) {
+      if (rg == 0) {
+#pragma unroll
+        for (int j = 0; j < QC; ++j) {
+          const float inv = 1.f / l[j];
+          float* o = p.out + ((int64_t)b * p.H + head0 + j) * D;
+#pragma unroll
+          for (int c = 0; c < NCH; ++c) {
+#pragma unroll
+            for (int v = 0; v < VEC; v += 2) {
+              float2 y;
+              y.x = acc[j][c * VEC + v] * inv;
+              y.y = acc[j][c * VEC + v + 1] * inv;
+              *reinterpret_cast<float2*>(o + (c * R + li) * VEC + v) = y;
+            }
+          }
+          if (p.lse && li == 0) p.lse[(int64_t)b * p.H + head0 + j] = (m[j] + __log2f(l[j])) * kLn2;
+        }
+      }
+    } else {
+      const int ord = seg_count == 0 ? 0 : 1;
+      const int64_t pstride = (int64_t)QC * (D + 2);
+      float* mine = p.partials + ((cta * 2 + ord) * NS + slot) * pstride;
+      if (rg == 0) {
+#pragma unroll
+        for (int j = 0; j < QC; ++j) {
+#pragma unroll
+          for (int c = 0; c < NCH; ++c)
+#pragma unroll
+            for (int v = 0; v < VEC; ++v) mine[j * D + (c * R + li) * VEC + v] = acc[j][c * VEC + v];
+          if (li == 0) {
+            mine[QC * D + j] = m[j];
+            mine[QC * D + QC + j] = l[j];
+          }
+        }
+      }
+      __threadfence();
+      __syncwarp();
+      int old = 0;
+      if (lane == 0) old = atomicAdd(&p.counters[((int64_t)gc * p.B + b) * NS + slot], 1);
+      old = __shfl_sync(0xffffffffu, old, 0);
+      const int64_t first = cta_of(h.seq_t0, T_all, p.N);
+      const int64_t last = cta_of(h.seq_t1 - 1, T_all, p.N);
+      if (old == (int)(last - first)) {
+        // this warp finished the sequence last: merge every piece of it
+        __threadfence();
+        float mg[QC], lg[QC];
+#pragma unroll
+        for (int j = 0; j < QC; ++j) { mg[j] = kNegBig; lg[j] = 0.f; }
+        for (int64_t c = first; c <= last; ++c) {
+          const int o2 = cta_lo(c, T_all, p.N) >= h.seq_t0 ? 0 : 1;
+          const float* pc = p.partials + ((c * 2 + o2) * NS + slot) * pstride;
+#pragma unroll
+          for (int j = 0; j < QC; ++j) mg[j] = fmaxf(mg[j], __ldcg(pc + QC * D + j));
+        }
+        constexpr int PER = QC * D / 32;
+        float o[PER];
+#pragma unroll
+        for (int k = 0; k < PER; ++k) o[k] = 0.f;
+        for (int64_t c = first; c <= last; ++c) {
+          const int o2 = cta_lo(c, T_all, p.N) >= h.seq_t0 ? 0 : 1;
+          const float* pc = p.partials + ((c * 2 + o2) * NS + slot) * pstride;
+          float w[QC];
+#pragma unroll
+          for (int j = 0; j < QC; ++j) {
+            w[j] = fast_exp2(__ldcg(pc + QC * D + j) - mg[j]);
+            lg[j] += __ldcg(pc + QC * D + QC + j) * w[j];
+          }
+#pragma unroll
+          for (int k = 0; k < PER; ++k) o[k] += __ldcg(pc + lane + 32 * k) * w[(32 * k) / D];
+        }
+#pragma unroll
+        for (int k = 0; k < PER; ++k) {
+          const int j = (32 * k) / D;
+          const int e = (lane + 32 * k) - j * D;
+          p.out[((int64_t)b * p.H + head0 + j) * D + e] = o[k] / lg[j];
+        }
+        if (p.lse && lane < QC) {
+#pragma unroll
+          for (int j = 0; j < QC; ++j)
+            if (lane == j) p.lse[(int64_t)b * p.H + head0 + j] = (mg[j] + __log2f(lg[j])) * kLn2;
+        }
+      }
+    }
+    ++seg_count;
+  }
+}
+
+}  // namespace decode
+
+// Kernel pointer for an instantiation (nullptr if not instantiated).
+const void* decode_kernel_ptr(int dtype, int D, int QC);
+int decode_max_warps(int dtype, int D, int QC);
+int decode_elems_per_lane(int dtype, int D);
+
+}  // namespace pa
+
+namespace pa {
+namespace decode {
+
+template <typename T, int D, int QC>
+const void* kernel_if_fits() {
+  if constexpr (QC * Geo<T, D>::EPL <= (sizeof(T) == 2 ? 64 : (sizeof(T) == 4 ? 32 : 16))) {
+    return reinterpret_cast<const void*>(&decode_kernel<T, D, QC>);
+  } else {
+    return nullptr;
+  }
+}
+
+template <typename T, int D>
+const void* pick_qc(int QC) {
+  switch (QC) {
+    case 1: return kernel_if_fits<T, D, 1>();
+    case 2: return kernel_if_fits<T, D, 2>();
+    case 4: return kernel_if_fits<T, D, 4>();
+    case 8: return kernel_if_fits<T, D, 8>();
+    default: return nullptr;
+  }
+}
+
+template <typename T>
+const void* pick_kernel(int D, int QC) {
+  switch (D) {
+    case 32: return pick_qc<T, 32>(QC);
+    case 64: return pick_qc<T, 64>(QC);
+    case 128: return pick_qc<T, 128>(QC);
+    case 256: return pick_qc<T, 256>(QC);
+    default: return nullptr;
+  }
+}
+
+}  // namespace decode
+}  // namespace pa

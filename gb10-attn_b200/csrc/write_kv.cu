@@ -1,0 +1,208 @@
+// write_kv.cu -- KV-pool writer (C ABI pa_write_kv).
+//
+// Replaces hetero-serve TorchBlockAllocator.write_kv(block_ids, start, k, v)
+// (heteroserve/kv/torch_blocks.py:92, un-vendored; behaviour from the call
+// sites harness/repro_crash.py:52-58 and gb10-attn docs/REPORT.md:141-179):
+// token t of the source, at sequence position p = start + t, goes to row
+// p % BS of block block_ids[p / BS] of every layer's K and V pool, for every
+// kv head, converted to the pool dtype with round-to-nearest-even.
+//
+// The reference did this with torch indexing on one [n_layer, 2, NB, BS, H, D]
+// tensor and faulted once that tensor passed 2^31 elements
+// (gb10-attn README.md:109-132).  Here every offset is 64-bit and each layer's
+// K and V are separate base pointers (monolithic pool views or one tensor per
+// layer alike), in one launch for all layers.
+//
+// Memory-bound gather/scatter: each thread moves 8 elements of one
+// (layer, K|V, token, head) row, 16-byte vector stores into the pool.
+#include <algorithm>
+
+#include "common.cuh"
+
+namespace pa {
+namespace writekv {
+
+constexpr int kMaxLayers = 64;  // layers per launch; more are split on the host
+
+struct Params {
+  char* k_layers[kMaxLayers];
+  char* v_layers[kMaxLayers];
+  const char* k_src;
+  const char* v_src;
+  int64_t src_layer_stride, src_head_stride, src_token_stride;  // elements
+  const int32_t* block_ids;
+  int64_t n_ids;
+  int64_t start, T, L, HKV, D, BS, NB;
+  int32_t* dev_status;
+};
+
+template <typename S>
+__device__ __forceinline__ float to_f32(S x);
+template <> __device__ __forceinline__ float to_f32<float>(float x) { return x; }
+template <> __device__ __forceinline__ float to_f32<__half>(__half x) { return __half2float(x); }
+template <> __device__ __forceinline__ float to_f32<__nv_bfloat16>(__nv_bfloat16 x) {
+  return __bfloat162float(x);
+}
+
+template <typename P>
+__device__ __forceinline__ P from_f32(float x);
+template <> __device__ __forceinline__ float from_f32<float>(float x) { return x; }
+template <> __device__ __forceinline__ double from_f32<double>(float x) { return (double)x; }
+template <> __device__ __forceinline__ __half from_f32<__half>(float x) { return __float2half_rn(x); }
+template <> __device__ __forceinline__ __nv_bfloat16 from_f32<__nv_bfloat16>(float x) {
+  return __float2bfloat16_rn(x);
+}
+
+// VEC: 8 elements per thread with vector loads/stores (needs D % 8 == 0 and
+// 16-byte aligned rows); otherwise one element per thread.
+template <typename S, typename P, bool VEC>
+__global__ void __launch_bounds__(256) write_kv_kernel(const __grid_constant__ Params p) {
+  constexpr int E = VEC ? 8 : 1;
+  const int64_t per_row = p.D / E;
+  const int64_t rows = p.L * 2 * p.T * p.HKV;
+  const int64_t total = rows * per_row;
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += stride) {
+    const int64_t chunk = i % per_row;
+    int64_t row = i / per_row;
+    const int64_t h = row % p.HKV;
+    row /= p.HKV;
+    const int64_t t = row % p.T;
+    row /= p.T;
+    const int kv = (int)(row % 2);
+    const int64_t l = row / 2;
+
+    const int64_t pos = p.start + t;
+    const int64_t page = pos / p.BS;
+    if (page >= p.n_ids) {
+      if (chunk == 0) report(p.dev_status, PA_DEVERR_BLOCK_ID);
+      continue;
+    }
+    const int64_t blk = p.block_ids[page];
+    if (blk < 0 || blk >= p.NB) {
+      if (chunk == 0) report(p.dev_status, PA_DEVERR_BLOCK_ID);
+      continue;
+    }
+    const S* src = reinterpret_cast<const S*>(kv ? p.v_src : p.k_src) + l * p.src_layer_stride +
+                   h * p.src_head_stride + t * p.src_token_stride + chunk * E;
+    P* dst = reinterpret_cast<P*>(kv ? p.v_layers[l] : p.k_layers[l]) +
+             ((blk * p.BS + (pos - page * p.BS)) * p.HKV + h) * p.D + chunk * E;
+    if constexpr (VEC) {
+      float f[8];
+      if constexpr (sizeof(S) == 4) {
+        const float4 a = reinterpret_cast<const float4*>(src)[0];
+        const float4 b = reinterpret_cast<const float4*>(src)[1];
+        f[0] = a.x; f[1] = a.y; f[2] = a.z; f[3] = a.w;
+        f[4] = b.x; f[5] = b.y; f[6] = b.z; f[7] = b.w;
+      } else {
+        const uint4 u = *reinterpret_cast<const uint4*>(src);
+        const S* s8 = reinterpret_cast<const S*>(&u);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) f[e] = to_f32<S>(s8[e]);
+      }
+      if constexpr (sizeof(P) == 2) {
+        uint4 u;
+        P* d8 = reinterpret_cast<P*>(&u);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) d8[e] = from_f32<P>(f[e]);
+        *reinterpret_cast<uint4*>(dst) = u;
+      } else if constexpr (sizeof(P) == 4) {
+        reinterpret_cast<float4*>(dst)[0] = make_float4(f[0], f[1], f[2], f[3]);
+        reinterpret_cast<float4*>(dst)[1] = make_float4(f[4], f[5], f[6], f[7]);
+      } else {
+#pragma unroll
+        for (int e = 0; e < 8; e += 2)
+          reinterpret_cast<double2*>(dst)[e / 2] = make_double2((double)f[e], (double)f[e + 1]);
+      }
+    } else {
+      *dst = from_f32<P>(to_f32<S>(*src));
+    }
+  }
+}
+
+template <typename S, typename P>
+static int launch_typed(const Params& p, bool vec, cudaStream_t s) {
+  const int64_t per_row = vec ? p.D / 8 : p.D;
+  const int64_t total = p.L * 2 * p.T * p.HKV * per_row;
+  if (total == 0) return PA_OK;
+  int sms = 148;
+  if (device_sm_count(&sms) != PA_OK) return PA_ERR_NO_DEVICE;
+  const int64_t blocks = std::max<int64_t>(1, std::min<int64_t>((total + 255) / 256, (int64_t)sms * 16));
+  if (vec)
+    write_kv_kernel<S, P, true><<<(unsigned)blocks, 256, 0, s>>>(p);
+  else
+    write_kv_kernel<S, P, false><<<(unsigned)blocks, 256, 0, s>>>(p);
+  return cuda_status(cudaGetLastError());
+}
+
+template <typename S>
+static int launch_src(const Params& p, int pool_dtype, bool vec, cudaStream_t s) {
+  switch (pool_dtype) {
+    case PA_DTYPE_F16: return launch_typed<S, __half>(p, vec, s);
+    case PA_DTYPE_BF16: return launch_typed<S, __nv_bfloat16>(p, vec, s);
+    case PA_DTYPE_F32: return launch_typed<S, float>(p, vec, s);
+    case PA_DTYPE_F64: return launch_typed<S, double>(p, vec, s);
+    default: return PA_ERR_DTYPE;
+  }
+}
+
+}  // namespace writekv
+}  // namespace pa
+
+extern "C" int pa_write_kv(void* const* k_layers, void* const* v_layers, int pool_dtype,
+                           const void* k_src, const void* v_src, int src_dtype,
+                           int64_t src_layer_stride, int64_t src_head_stride,
+                           int64_t src_token_stride, const int32_t* block_ids,
+                           int64_t num_block_ids, int64_t start, int64_t num_tokens,
+                           int64_t num_layers, int64_t num_kv_heads, int64_t head_dim,
+                           int64_t block_size, int64_t num_blocks, int32_t* dev_status,
+                           void* stream) {
+  using namespace pa;
+  using writekv::kMaxLayers;
+  if (num_tokens < 0 || num_layers < 0 || num_kv_heads <= 0 || head_dim <= 0 ||
+      block_size <= 0 || num_blocks < 0 || start < 0 || num_block_ids < 0)
+    return PA_ERR_INVALID_ARGUMENT;
+  if (num_tokens == 0 || num_layers == 0) return PA_OK;
+  if (!k_layers || !v_layers || !k_src || !v_src || !block_ids) return PA_ERR_INVALID_ARGUMENT;
+  if (src_dtype != PA_DTYPE_F32 && src_dtype != PA_DTYPE_F16 && src_dtype != PA_DTYPE_BF16)
+    return PA_ERR_DTYPE;
+  const int ps = dtype_size(pool_dtype), ss = dtype_size(src_dtype);
+  if (ps == 0) return PA_ERR_DTYPE;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  for (int64_t l0 = 0; l0 < num_layers; l0 += kMaxLayers) {
+    const int64_t nl = std::min<int64_t>(kMaxLayers, num_layers - l0);
+    writekv::Params p = {};
+    bool vec = (head_dim % 8 == 0) && aligned16(k_src) && aligned16(v_src) &&
+               (src_layer_stride * ss) % 16 == 0 && (src_head_stride * ss) % 16 == 0 &&
+               (src_token_stride * ss) % 16 == 0 && (head_dim * ps) % 16 == 0;
+    for (int64_t l = 0; l < nl; ++l) {
+      p.k_layers[l] = static_cast<char*>(k_layers[l0 + l]);
+      p.v_layers[l] = static_cast<char*>(v_layers[l0 + l]);
+      if (!p.k_layers[l] || !p.v_layers[l]) return PA_ERR_INVALID_ARGUMENT;
+      vec = vec && aligned16(p.k_layers[l]) && aligned16(p.v_layers[l]);
+    }
+    p.k_src = static_cast<const char*>(k_src) + l0 * src_layer_stride * ss;
+    p.v_src = static_cast<const char*>(v_src) + l0 * src_layer_stride * ss;
+    p.src_layer_stride = src_layer_stride;
+    p.src_head_stride = src_head_stride;
+    p.src_token_stride = src_token_stride;
+    p.block_ids = block_ids;
+    p.n_ids = num_block_ids;
+    p.start = start;
+    p.T = num_tokens;
+    p.L = nl;
+    p.HKV = num_kv_heads;
+    p.D = head_dim;
+    p.BS = block_size;
+    p.NB = num_blocks;
+    p.dev_status = dev_status;
+    int st;
+    switch (src_dtype) {
+      case PA_DTYPE_F32: st = writekv::launch_src<float>(p, pool_dtype, vec, s); break;
+      case PA_DTYPE_F16: st = writekv::launch_src<__half>(p, pool_dtype, vec, s); break;
+      default: st = writekv::launch_src<__nv_bfloat16>(p, pool_dtype, vec, s); break;
+    }
+    if (st) return st;
+  }
+  return PA_OK;
+}

@@ -1,0 +1,93 @@
+"""The C ABI library on CPU: it loads, exports every entry point the header
+declares, and rejects bad arguments before touching a device."""
+from __future__ import annotations
+
+import ctypes
+
+import pytest
+
+from pa_b200 import _lib
+
+
+def test_library_loads_and_version():
+    lib = _lib.load()
+    assert lib.pa_abi_version() == 1
+
+
+def test_exports_every_header_symbol():
+    declared = _lib.header_symbols()
+    assert len(declared) >= 15
+    lib = _lib.load()
+    missing = [s for s in declared if not hasattr(lib, s)]
+    assert not missing, missing
+    # and the ctypes table covers every declared entry point
+    assert set(declared) <= set(_lib.SIGNATURES), set(declared) - set(_lib.SIGNATURES)
+
+
+def test_strerror_table():
+    for code in range(0, 11):
+        assert _lib.strerror(code) != "unknown status"
+    assert _lib.strerror(999) == "unknown status"
+    assert _lib.strerror(_lib.PA_ERR_NUM_HEADS) == "n_head must be divisible by n_kv_head"
+
+
+@pytest.mark.parametrize("H,HKV,D,dt,want", [
+    (12, 5, 64, _lib.PA_DTYPE_F16, _lib.PA_ERR_NUM_HEADS),
+    (12, 12, 48, _lib.PA_DTYPE_F16, _lib.PA_ERR_HEAD_DIM),
+    (12, 12, 64, 17, _lib.PA_ERR_DTYPE),
+    (0, 12, 64, _lib.PA_DTYPE_F16, _lib.PA_ERR_INVALID_ARGUMENT),
+])
+def test_workspace_query_validates_before_device(H, HKV, D, dt, want):
+    n = ctypes.c_size_t(0)
+    st = _lib.call("pa_decode_workspace_size", 4, H, HKV, D, dt, 16, 128, 0, ctypes.byref(n))
+    assert st == want
+
+
+def test_no_device_is_reported_not_crashed():
+    import torch
+    if torch.cuda.is_available():
+        pytest.skip("a device is present")
+    n = ctypes.c_size_t(0)
+    st = _lib.call("pa_decode_workspace_size", 4, 12, 12, 64, _lib.PA_DTYPE_F16, 16, 128, 0,
+                   ctypes.byref(n))
+    assert st == _lib.PA_ERR_NO_DEVICE
+    assert _lib.call("pa_choose_num_splits", 4, 12, 2048) == -1
+
+
+def test_empty_batch_is_a_no_op():
+    n = ctypes.c_size_t(123)
+    assert _lib.call("pa_decode_workspace_size", 0, 12, 12, 64, _lib.PA_DTYPE_F16, 16, 128, 0,
+                     ctypes.byref(n)) == 0
+    assert n.value == 0
+    # B = 0: no pointer is touched, nothing launched
+    st = _lib.call("pa_paged_attention_v3", None, None, None, None, None, _lib.PA_DTYPE_F16,
+                   None, None, 0, 12, 12, 64, 16, 10, 4, 0.125, 0, None, 0, None, None)
+    assert st == 0
+
+
+def test_write_kv_argument_checks():
+    st = _lib.call("pa_write_kv", None, None, _lib.PA_DTYPE_F16, None, None, 9, 0, 0, 0, None,
+                   4, 0, 10, 1, 12, 64, 16, 10, None, None)
+    assert st == _lib.PA_ERR_INVALID_ARGUMENT  # null pointers with work to do
+    st = _lib.call("pa_write_kv", None, None, _lib.PA_DTYPE_F16, None, None, 9, 0, 0, 0, None,
+                   4, 0, 0, 1, 12, 64, 16, 10, None, None)
+    assert st == 0  # zero tokens: nothing to do
+
+
+def test_torch_shim_imports_on_cpu():
+    from pa_b200 import ops
+    assert ops.shim_path().exists()
+    for name in ("paged_attention", "paged_attention_v2", "paged_attention_v3",
+                 "choose_num_splits", "paged_attention_prefill", "paged_attention_prefill_wmma",
+                 "write_kv"):
+        assert callable(getattr(ops, name))
+
+
+def test_shim_rejects_cpu_tensors_like_the_reference():
+    import torch
+    from pa_b200 import ops
+    q = torch.zeros(1, 2, 32)
+    k = torch.zeros(4, 16, 2, 32, dtype=torch.float16)
+    with pytest.raises(RuntimeError, match="q must be on CUDA"):
+        ops.paged_attention_v3(q, k, k, torch.zeros(1, 1, dtype=torch.int32),
+                               torch.ones(1, dtype=torch.int32), 0.1, 0)

@@ -1,0 +1,68 @@
+"""Causal chunked prefill on the GPU against the oracle (max-abs 2e-3)."""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+
+from abi_helpers import abi_prefill, max_abs, to_dev
+from oracle import oracle as orc
+
+pytestmark = pytest.mark.gpu
+
+
+def case(seed, B, Sq, H, HKV, D, BS, ctx, dtype):
+    _, k, v, bt, c = orc.make_decode_case(seed, B, H, HKV, D, BS, ctx)
+    q = np.random.default_rng(seed + 1000).standard_normal((B, Sq, H, D), dtype=np.float32)
+    return q, orc.round_to(k, dtype), orc.round_to(v, dtype), bt, c
+
+
+@pytest.mark.parametrize("entry", ["pa_paged_attention_prefill", "pa_paged_attention_prefill_simt",
+                                   "pa_paged_attention_prefill_wmma"])
+@pytest.mark.parametrize("dtype", ["float16", "bfloat16"])
+@pytest.mark.parametrize("D", [64, 128])
+def test_prefill_tensor_dtypes(entry, dtype, D):
+    q, k, v, bt, ctx = case(30 + D, 2, 96, 8, 2, D, 16, [96, 300], dtype)
+    out = abi_prefill(q, k, v, bt, ctx, D ** -0.5, dtype, entry=entry)
+    assert max_abs(out, orc.prefill(q, k, v, bt, ctx, D ** -0.5, threads=8)) <= 2e-3
+
+
+@pytest.mark.parametrize("dtype,D,BS", [("float32", 64, 16), ("float64", 32, 8),
+                                        ("float16", 256, 16), ("float32", 128, 5)])
+def test_prefill_cuda_core_dtypes(dtype, D, BS):
+    q, k, v, bt, ctx = case(40, 2, 33, 4, 4, D, BS, [40, 33], dtype)
+    out = abi_prefill(q, k, v, bt, ctx, D ** -0.5, dtype)
+    tol = 2e-3 if dtype in ("float16", "bfloat16") else 1e-4
+    assert max_abs(out, orc.prefill(q, k, v, bt, ctx, D ** -0.5)) <= tol
+
+
+def test_padded_query_slots_are_zero():
+    # Sq > ctx: the first Sq - ctx slots see no key (paged_attn_prefill.cu:70-74)
+    q, k, v, bt, ctx = case(41, 2, 40, 4, 2, 64, 16, [10, 64], "float16")
+    out = abi_prefill(q, k, v, bt, ctx, 0.125, "float16")
+    assert np.all(out[0, :30] == 0)
+    assert max_abs(out, orc.prefill(q, k, v, bt, ctx, 0.125)) <= 2e-3
+
+
+def test_chunk_after_cached_prefix():
+    # the chunk is the trailing 64 tokens of a 1000-token context
+    q, k, v, bt, ctx = case(42, 3, 64, 8, 8, 128, 16, [1000, 64, 513], "bfloat16")
+    out = abi_prefill(q, k, v, bt, ctx, 0.088, "bfloat16")
+    assert max_abs(out, orc.prefill(q, k, v, bt, ctx, 0.088, threads=8)) <= 2e-3
+
+
+def test_shim_prefill_and_wmma_checks():
+    import torch
+    from pa_b200 import ops
+    q, k, v, bt, ctx = case(43, 2, 32, 4, 2, 64, 16, [32, 50], "float16")
+    args = [to_dev(q), to_dev(k, "float16"), to_dev(v, "float16"), to_dev(bt), to_dev(ctx)]
+    ref = orc.prefill(q, k, v, bt, ctx, 0.125)
+    assert max_abs(ops.paged_attention_prefill(*args, 0.125).cpu().numpy(), ref) <= 2e-3
+    assert max_abs(ops.paged_attention_prefill_wmma(*args, 0.125).cpu().numpy(), ref) <= 2e-3
+    k32 = args[1].float()
+    with pytest.raises(RuntimeError, match="the WMMA path needs an fp16 KV cache"):
+        ops.paged_attention_prefill_wmma(args[0], k32, k32, *args[3:], 0.125)
+    k8 = torch.zeros((8, 8, 2, 64), dtype=torch.float16, device="cuda")
+    with pytest.raises(RuntimeError, match="block_size == 16"):
+        ops.paged_attention_prefill_wmma(args[0], k8, k8, *args[3:], 0.125)
+    with pytest.raises(RuntimeError, match=r"q must be \[B, S, H, D\]"):
+        ops.paged_attention_prefill(args[0][0], *args[1:], 0.125)
