@@ -46,9 +46,8 @@ sys.path.insert(0, str(REPO))
 
 METRIC = "decode achieved HBM GB/s (% of B200 peak), cold pools; tokens/s at 1/2/4/8 GPUs"
 
-# configs[1] geometry
-L, H, HKV, D, BS, B, CTX = 12, 12, 12, 64, 16, 64, 2048
-REGIONS = 4
+# configs[1] geometry (layers / regions can be reduced for profiler captures)
+H, HKV, D, BS, B, CTX = 12, 12, 64, 16, 64, 2048
 
 
 def _env_rank():
@@ -97,7 +96,7 @@ class ClockSampler:
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-                 "-i", str(self.idx), "-lms", "100"], stdout=subprocess.PIPE,
+                 "-i", str(self.idx), "-lms", "20"], stdout=subprocess.PIPE,
                 stderr=subprocess.DEVNULL, text=True)
             self.t = threading.Thread(target=self._read, daemon=True)
             self.t.start()
@@ -151,6 +150,7 @@ def run_b200(args) -> None:
 
     from pa_b200 import harness, ops
 
+    L, REGIONS = args.layers, args.regions
     rank, local, world = _env_rank()
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
@@ -161,7 +161,7 @@ def run_b200(args) -> None:
 
     gen = torch.Generator(device=dev)
     gen.manual_seed(1234 + rank)
-    nb = B * (CTX // BS) * REGIONS  # 32768 blocks per layer pool
+    nb = B * (CTX // BS) * REGIONS  # 32768 blocks per layer pool with 4 regions
     # one [2, NB, BS, HKV, D] tensor per layer (the reference's per-layer pool)
     pools = []
     for _ in range(L):
@@ -180,29 +180,16 @@ def run_b200(args) -> None:
     bytes_per_call = harness.decode_bytes(ctx_np, H, HKV, D, 2, BS)
     bytes_per_step = L * bytes_per_call
 
+    def layer_call(layer: int, q, bt, ctx):
+        return ops.paged_attention_v3(q, pools[layer][0], pools[layer][1], bt, ctx, scale, 0)
+
     def step(i: int):
         bt = bt_dev[i % REGIONS]
         for layer in range(L):
-            outs[layer] = ops.paged_attention_v3(q_dev[layer], pools[layer][0], pools[layer][1],
-                                                 bt, ctx_dev, scale, 0)
+            outs[layer] = layer_call(layer, q_dev[layer], bt, ctx_dev)
 
-    # correctness gate (the reference's bench checks every path before timing,
-    # docs/REPORT.md:41-43): layer 0 against a dense torch fp32 reference
-    bt0 = tables[0]
-    kf = pools[0][0].float()
-    vf = pools[0][1].float()
-    ref_err = 0.0
-    for b in range(0, B, 16):
-        blocks = torch.from_numpy(bt0[b, :CTX // BS].astype(np.int64)).to(dev)
-        kk = kf[blocks].reshape(CTX, HKV, D)
-        vv = vf[blocks].reshape(CTX, HKV, D)
-        s = torch.einsum("hd,thd->ht", q_dev[0, b], kk) * scale
-        want = torch.einsum("ht,thd->hd", torch.softmax(s, -1), vv)
-        got = ops.paged_attention_v3(q_dev[0, b:b + 1], pools[0][0], pools[0][1],
-                                     bt_dev[0][b:b + 1], ctx_dev[b:b + 1], scale, 0)[0]
-        ref_err = max(ref_err, float((got - want).abs().max()))
-    del kf, vf
-    torch.cuda.empty_cache()
+    ref_err = correctness_gate(torch, layer_call, pools[0], q_dev[0], tables[0], bt_dev[0],
+                               ctx_dev, scale, dev)
     if ref_err > 2e-3:
         raise SystemExit(f"correctness gate failed: max-abs {ref_err}")
 
@@ -226,34 +213,117 @@ def run_b200(args) -> None:
     t_ms = ev0.elapsed_time(ev1)
 
     # --- per-launch decode time (same stream, events around each call) -----
-    n_launch = min(L * 4, L * args.steps)
+    n_launch = min(L * 4, max(L * args.steps, 4))
     evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
            for _ in range(n_launch)]
     torch.cuda.synchronize()
     for j, (a, b_) in enumerate(evs):
         layer = j % L
         a.record(stream)
-        outs[layer] = ops.paged_attention_v3(q_dev[layer], pools[layer][0], pools[layer][1],
-                                             bt_dev[(j // L) % REGIONS], ctx_dev, scale, 0)
+        outs[layer] = layer_call(layer, q_dev[layer], bt_dev[(j // L) % REGIONS], ctx_dev)
         b_.record(stream)
     torch.cuda.synchronize()
     launch_ms = statistics.mean(a.elapsed_time(b_) for a, b_ in evs)
 
     # --- end to end through the public API with host buffers ---------------
-    q_host = torch.empty((L, B, H, D), dtype=torch.float32).pin_memory()
+    if args.no_e2e:
+        e2e_ms, h2d, d2h = float("nan"), 0, 0
+    else:
+        e2e_ms, h2d, d2h = run_e2e(torch, dist, args, layer_call, q_dev, tables, ctx_np, dev,
+                                   stream, world, L, REGIONS)
+
+    # max over ranks
+    times = torch.tensor([t_ms, e2e_ms, launch_ms], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(times, op=dist.ReduceOp.MAX)
+    t_ms, e2e_ms, launch_ms = (float(x) for x in times.cpu())
+
+    total_bytes = bytes_per_step * args.steps * world
+    value = total_bytes / (t_ms * 1e-3) / 1e9
+    e2e_val = total_bytes / (e2e_ms * 1e-3) / 1e9 if e2e_ms == e2e_ms else None
+    peaks = _peaks()
+    # decode-kernel roofline: bytes of one layer call / mean call time over the
+    # timed region (events on the launching stream; the call's plan kernel is
+    # included, so this is a lower bound on the kernel's own rate)
+    call_ms = t_ms / (args.steps * L)
+    achieved = bytes_per_call / (call_ms * 1e-3) / 1e9
+    traffic = _profile_traffic("decode_kernel")
+    clk = clocks.summary()
+
+    line = {
+        "metric": METRIC, "value": round(value, 1), "unit": "GB/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(t_ms / args.steps, 4), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f16",
+        "data": "synthetic N(0,1) KV pool and q, seeded",
+        "config": {"workload": f"configs[1]: gpt2 paged decode, {L} layers, B=64/GPU, ctx=2048, "
+                               "H=HKV=12, D=64, block_size=16, fp16 KV, fp32 q/out",
+                   "global_batch": B * world, "seq_len": CTX, "layers": L,
+                   "parallelism": f"batch-sharded x{world} (no collective)",
+                   "cold": f"{REGIONS} disjoint block regions rotated per step; inputs larger "
+                           f"than L2 ({bytes_per_step / 1e9:.2f} GB/step, "
+                           f"{REGIONS * bytes_per_step / 1e9:.1f} GB rotation)",
+                   "tokens_per_s": round(B * world * args.steps / (t_ms * 1e-3), 1),
+                   "pct_of_measured_hbm_peak": round(100 * value / world / peaks["hbm_gbs"], 1),
+                   "pct_of_spec_8TBs": round(100 * value / world / 8000.0, 1),
+                   "correctness_gate_max_abs": ref_err},
+        "e2e": {"value": round(e2e_val, 1) if e2e_val else None, "unit": "GB/s",
+                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                "tokens_per_s": round(B * world * args.steps / (e2e_ms * 1e-3), 1)
+                if e2e_val else None},
+        "gpu_launches": 2 * L * args.steps,
+        "roofline": {"bound": "hbm", "achieved": round(achieved, 1),
+                     "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                     "frac": round(achieved / peaks["hbm_gbs"], 4),
+                     "traffic": traffic, "peak_source": peaks["src"],
+                     "kernel": "pa::decode::decode_kernel<__half,64,1> (+ plan_kernel, PDL)",
+                     "bytes_per_launch": bytes_per_call,
+                     "launch_us": round(call_ms * 1e3, 2),
+                     "isolated_launch_us": round(launch_ms * 1e3, 2)},
+        "clocks": clk,
+    }
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        line["cpu_baseline"] = cpu_baseline(args.cpu_seconds)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+
+
+def correctness_gate(torch, layer_call, pool, q, bt_np, bt_dev, ctx_dev, scale, dev) -> float:
+    """The reference's bench checks each path before timing it
+    (docs/REPORT.md:41-43): here the full B=64 layer-0 call against a dense
+    torch fp32 gather + softmax reference."""
+    got = layer_call(0, q, bt_dev, ctx_dev)
+    blocks = torch.from_numpy(bt_np[:, :CTX // BS].astype(np.int64)).to(dev)
+    err = 0.0
+    for b0 in range(0, B, 8):
+        idx = blocks[b0:b0 + 8].reshape(-1)
+        kk = pool[0][idx].float().reshape(-1, CTX, HKV, D)
+        vv = pool[1][idx].float().reshape(-1, CTX, HKV, D)
+        s = torch.einsum("bhd,bthd->bht", q[b0:b0 + 8], kk) * scale
+        want = torch.einsum("bht,bthd->bhd", torch.softmax(s, -1), vv)
+        err = max(err, float((got[b0:b0 + 8] - want).abs().max()))
+    return err
+
+
+def run_e2e(torch, dist, args, layer_call, q_dev, tables, ctx_np, dev, stream, world, L,
+            REGIONS):
+    """Same decode steps through the public API with host buffers: q and the
+    block table copied host->device and the outputs device->host each step."""
+    q_host = torch.empty(tuple(q_dev.shape), dtype=torch.float32).pin_memory()
     q_host.copy_(q_dev.cpu())
     bt_host = [torch.from_numpy(t).pin_memory() for t in tables]
     ctx_host = torch.from_numpy(ctx_np).pin_memory()
-    out_host = torch.empty((L, B, H, D), dtype=torch.float32).pin_memory()
+    out_host = torch.empty(tuple(q_dev.shape), dtype=torch.float32).pin_memory()
 
     def e2e_step(i: int):
         qd = q_host.to(dev, non_blocking=True)
         btd = bt_host[i % REGIONS].to(dev, non_blocking=True)
         cd = ctx_host.to(dev, non_blocking=True)
         for layer in range(L):
-            o = ops.paged_attention_v3(qd[layer], pools[layer][0], pools[layer][1], btd, cd,
-                                       scale, 0)
-            out_host[layer].copy_(o, non_blocking=True)
+            out_host[layer].copy_(layer_call(layer, qd[layer], btd, cd), non_blocking=True)
 
     for i in range(max(2, args.warmup)):
         e2e_step(i)
@@ -266,61 +336,9 @@ def run_b200(args) -> None:
         e2e_step(i)
     e1.record(stream)
     torch.cuda.synchronize()
-    e2e_ms = e0.elapsed_time(e1)
     h2d = q_host.numel() * 4 + bt_host[0].numel() * 4 + ctx_host.numel() * 4
     d2h = out_host.numel() * 4
-
-    # max over ranks
-    times = torch.tensor([t_ms, e2e_ms, launch_ms], dtype=torch.float64, device=dev)
-    if world > 1:
-        dist.all_reduce(times, op=dist.ReduceOp.MAX)
-    t_ms, e2e_ms, launch_ms = (float(x) for x in times.cpu())
-
-    total_bytes = bytes_per_step * args.steps * world
-    value = total_bytes / (t_ms * 1e-3) / 1e9
-    e2e_val = total_bytes / (e2e_ms * 1e-3) / 1e9
-    peaks = _peaks()
-    achieved = bytes_per_call / (launch_ms * 1e-3) / 1e9
-    traffic = _profile_traffic("decode_kernel")
-    clk = clocks.summary()
-
-    line = {
-        "metric": METRIC, "value": round(value, 1), "unit": "GB/s", "n_gpus": world,
-        "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": round(t_ms / args.steps, 4), "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "f16",
-        "data": "synthetic N(0,1) KV pool and q, seeded",
-        "config": {"workload": "configs[1]: gpt2 paged decode, 12 layers, B=64/GPU, ctx=2048, "
-                               "H=HKV=12, D=64, block_size=16, fp16 KV, fp32 q/out",
-                   "global_batch": B * world, "seq_len": CTX, "layers": L,
-                   "parallelism": f"batch-sharded x{world} (no collective)",
-                   "cold": f"{REGIONS} disjoint block regions rotated per step; inputs larger "
-                           f"than L2 ({bytes_per_step / 1e9:.2f} GB/step, "
-                           f"{REGIONS * bytes_per_step / 1e9:.1f} GB rotation)",
-                   "tokens_per_s": round(B * world * args.steps / (t_ms * 1e-3), 1),
-                   "pct_of_measured_hbm_peak": round(100 * value / world / peaks["hbm_gbs"], 1),
-                   "pct_of_spec_8TBs": round(100 * value / world / 8000.0, 1),
-                   "correctness_gate_max_abs": ref_err},
-        "e2e": {"value": round(e2e_val, 1), "unit": "GB/s", "h2d_bytes_per_step": h2d,
-                "d2h_bytes_per_step": d2h,
-                "tokens_per_s": round(B * world * args.steps / (e2e_ms * 1e-3), 1)},
-        "gpu_launches": 2 * L * args.steps,
-        "roofline": {"bound": "hbm", "achieved": round(achieved, 1),
-                     "peak": peaks["hbm_gbs"], "unit": "GB/s",
-                     "frac": round(achieved / peaks["hbm_gbs"], 4),
-                     "traffic": traffic, "peak_source": peaks["src"],
-                     "kernel": "pa::decode::decode_kernel<__half,64,1> (+ plan_kernel, PDL)",
-                     "bytes_per_launch": bytes_per_call,
-                     "launch_us": round(launch_ms * 1e3, 2)},
-        "clocks": clk,
-    }
-    if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        line["cpu_baseline"] = cpu_baseline(args.cpu_seconds)
-    if world > 1:
-        dist.barrier()
-        dist.destroy_process_group()
-    if rank == 0:
-        print(json.dumps(line), flush=True)
+    return e0.elapsed_time(e1), h2d, d2h
 
 
 # ---------------------------------------------------------------------------
@@ -391,12 +409,15 @@ def run_reference(args) -> None:
 def main() -> None:
     ap = argparse.ArgumentParser(description=__doc__.split("\n")[0])
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
-    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--ref-step-seconds", type=float, default=3.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--layers", type=int, default=12, help="fewer layers: profiler captures only")
+    ap.add_argument("--regions", type=int, default=4, help="cold block regions in rotation")
+    ap.add_argument("--no-e2e", action="store_true", help="skip the host-buffer e2e leg")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

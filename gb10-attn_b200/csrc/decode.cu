@@ -80,7 +80,12 @@ struct PlanParams {
 // counters; the sequence holding each CTA's first tile; NaN rows for empty
 // sequences (the reference's v3 yields NaN there, paged_attn_v3.cu:160-165).
 __global__ void __launch_bounds__(kPlanThreads) plan_kernel(const __grid_constant__ PlanParams pp) {
+  // Launched with programmatic stream serialisation: let the decode kernel
+  // start launching at once, and wait for the previous kernel on the stream
+  // (which may still use this workspace or write context_lens) before
+  // touching memory.
   pdl_trigger();
+  pdl_wait();
   __shared__ int32_t warp_tot[kPlanThreads / 32];
   __shared__ int32_t carry_s;
   const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
@@ -137,7 +142,7 @@ __global__ void __launch_bounds__(kPlanThreads) plan_kernel(const __grid_constan
   const int64_t Tpg = carry_s;
   const int64_t T_all = Tpg * pp.NGC;
   for (int64_t c = tid; c < pp.N; c += kPlanThreads) {
-    const int64_t lo = c * T_all / pp.N;
+    const int64_t lo = cta_lo(c, T_all, pp.N);
     int32_t seq = 0;
     if (lo < T_all) {
       const int64_t r = lo % Tpg;
@@ -156,6 +161,27 @@ __global__ void __launch_bounds__(kPlanThreads) plan_kernel(const __grid_constan
 
 static std::mutex g_mu;
 
+// Opt a kernel into the large dynamic shared-memory carve-out, once per
+// (device, kernel).  Caller holds g_mu.
+static int ensure_smem_attr_locked(int dev, const void* kernel) {
+  static std::vector<std::pair<int, const void*>> done;
+  for (auto& a : done)
+    if (a.first == dev && a.second == kernel) return PA_OK;
+  cudaError_t e =
+      cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+  if (e != cudaSuccess) return cuda_status(e);
+  done.push_back({dev, kernel});
+  return PA_OK;
+}
+
+static int ensure_smem_attr(const void* kernel) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_status(e);
+  std::lock_guard<std::mutex> lk(g_mu);
+  return ensure_smem_attr_locked(dev, kernel);
+}
+
 // Blocks per SM for (kernel, threads, smem); sets the dynamic smem limit once
 // per (device, kernel).
 static int occupancy(const void* kernel, int threads, size_t smem, int* blocks) {
@@ -167,7 +193,6 @@ static int occupancy(const void* kernel, int threads, size_t smem, int* blocks) 
     int blocks;
   };
   static std::vector<Key> cache;
-  static std::vector<std::pair<int, const void*>> attr_set;
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return cuda_status(e);
@@ -177,13 +202,8 @@ static int occupancy(const void* kernel, int threads, size_t smem, int* blocks) 
       *blocks = k.blocks;
       return PA_OK;
     }
-  bool have_attr = false;
-  for (auto& a : attr_set) have_attr |= (a.first == dev && a.second == kernel);
-  if (!have_attr) {
-    e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
-    if (e != cudaSuccess) return cuda_status(e);
-    attr_set.push_back({dev, kernel});
-  }
+  int st = ensure_smem_attr_locked(dev, kernel);
+  if (st) return st;
   int nb = 0;
   e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&nb, kernel, threads, smem);
   if (e != cudaSuccess) return cuda_status(e);
@@ -283,6 +303,8 @@ int launch(const DecodeArgs& a, void* ws, size_t ws_bytes, cudaStream_t stream) 
   st = configure(a, &c);
   if (st) return st;
   if (!ws || ws_bytes < c.total || !aligned16(ws)) return PA_ERR_WORKSPACE;
+  st = ensure_smem_attr(c.kernel);
+  if (st) return st;
 
   char* w = static_cast<char*>(ws);
   PlanParams pp;
@@ -303,8 +325,16 @@ int launch(const DecodeArgs& a, void* ws, size_t ws_bytes, cudaStream_t stream) 
   pp.NGC = c.NGC;
   pp.N = c.N;
   pp.empty_fill = a.empty_fill;
-  plan_kernel<<<1, kPlanThreads, 0, stream>>>(pp);
-  cudaError_t e = cudaGetLastError();
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cudaLaunchConfig_t pcfg = {};
+  pcfg.gridDim = dim3(1);
+  pcfg.blockDim = dim3(kPlanThreads);
+  pcfg.stream = stream;
+  pcfg.attrs = attr;
+  pcfg.numAttrs = 1;
+  cudaError_t e = cudaLaunchKernelEx(&pcfg, plan_kernel, pp);
   if (e != cudaSuccess) return cuda_status(e);
 
   Params p;
@@ -336,6 +366,7 @@ int launch(const DecodeArgs& a, void* ws, size_t ws_bytes, cudaStream_t stream) 
   p.nstage = c.nstage;
   p.qscale = (float)a.scale * kLog2e;
   p.row_bytes = c.row_bytes;
+  p.rows_contiguous = (c.G == a.HKV) ? 1 : 0;
   const int elt = dtype_size(a.dtype);
   p.tok_stride = a.HKV * a.D * elt;
   p.blk_stride = a.BS * p.tok_stride;
@@ -345,9 +376,6 @@ int launch(const DecodeArgs& a, void* ws, size_t ws_bytes, cudaStream_t stream) 
   cfg.blockDim = dim3((unsigned)c.threads);
   cfg.dynamicSmemBytes = c.smem;
   cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   void* args[] = {&p};

@@ -61,6 +61,7 @@ struct Params {
   int32_t G, QPK, NS, NGC, N, nstage;
   float qscale;                  // scale * log2(e)
   uint32_t row_bytes;            // G * D * sizeof(T)
+  int32_t rows_contiguous;       // G == HKV: a page's token rows are adjacent
   int64_t tok_stride;            // HKV * D * sizeof(T): one token row of a page
   int64_t blk_stride;            // BS * tok_stride: one page
 };
@@ -106,12 +107,16 @@ constexpr int kProdRegs = 48;
 constexpr int kConsRegs = 224;
 static_assert(128 * kProdRegs + 256 * kConsRegs <= 384 * 168, "register split exceeds launch");
 
-__device__ __forceinline__ int64_t cta_lo(int64_t c, int64_t T_all, int64_t N) {
-  return c * T_all / N;
+// First global tile of CTA c.  With at least as many tiles as CTAs the
+// ranges are floor(c * T / N) (never empty); with fewer, CTA c takes tile c and
+// the CTAs past T are empty -- so the CTAs holding any one sequence are always
+// consecutive AND non-empty, which the last-arriver merge count relies on.
+__host__ __device__ __forceinline__ int64_t cta_lo(int64_t c, int64_t T_all, int64_t N) {
+  return T_all >= N ? c * T_all / N : (c < T_all ? c : T_all);
 }
-// CTA whose range holds global tile t: the largest c with cta_lo(c) <= t.
-__device__ __forceinline__ int64_t cta_of(int64_t t, int64_t T_all, int64_t N) {
-  return ((t + 1) * N - 1) / T_all;
+// CTA whose range holds global tile t < T_all: the largest c with cta_lo(c) <= t.
+__host__ __device__ __forceinline__ int64_t cta_of(int64_t t, int64_t T_all, int64_t N) {
+  return T_all >= N ? ((t + 1) * N - 1) / T_all : t;
 }
 
 template <typename T, int D, int QC>
@@ -141,7 +146,10 @@ __global__ void __launch_bounds__(Limits<T, D, QC>::THREADS, 1)
   }
   __syncthreads();
   // Everything above overlaps the plan kernel; its tables are read below.
+  // The next call's plan kernel may launch now: it waits for this grid to
+  // complete before it touches memory.
   pdl_wait();
+  pdl_trigger();
 
   const int64_t Tpg = p.tile_off[p.B];  // tiles per g-chunk
   const int64_t T_all = Tpg * p.NGC;
@@ -239,7 +247,18 @@ __global__ void __launch_bounds__(Limits<T, D, QC>::THREADS, 1)
                             off * p.tok_stride + (int64_t)gc * gbytes;
           unsigned char* dst = smem + (size_t)stage * stage_bytes +
                                (size_t)(kv * kTT + row) * p.row_bytes;
-          bulk_g2s(dst, src, p.row_bytes, &full[stage]);
+          if (p.rows_contiguous) {
+            // The g-chunk spans every KV head, so the tile's rows that share a
+            // page are one contiguous run of bytes: one bulk copy per run,
+            // issued by the run's first row (one K + one V copy per tile when
+            // 16 | block_size).
+            if (row == 0 || off == 0) {
+              const int64_t run = min((int64_t)(nvalid - row), p.BS - off);
+              bulk_g2s(dst, src, (uint32_t)run * p.row_bytes, &full[stage]);
+            }
+          } else {
+            bulk_g2s(dst, src, p.row_bytes, &full[stage]);
+          }
         }
 
         ++gt;

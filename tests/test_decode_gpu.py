@@ -122,7 +122,7 @@ def test_out_of_range_block_ids_are_reported_not_read():
     out = abi_decode(q, k, v, bt, ctx, 0.125, "float16", status=status)
     assert int(status.item()) & _lib.PA_DEVERR_BLOCK_ID
     # sequence 0 is untouched by the bad entry
-    assert max_abs(out[0], orc.decode(q, k, v, bt[:1], ctx[:1], 0.125)[0]) <= 2e-3
+    assert max_abs(out[0], orc.decode(q[:1], k, v, bt[:1], ctx[:1], 0.125)[0]) <= 2e-3
 
 
 def test_context_longer_than_table_is_clamped_and_reported():
