@@ -44,9 +44,11 @@ def gather_states(out: torch.Tensor, lse: torch.Tensor, group=None
     returns outs [R,B,H,D], lses [R,B,H] in rank order (one collective)."""
     world = dist.get_world_size(group)
     packed = pack_state(out.float(), lse.float())
-    buf = torch.empty((world, *packed.shape), dtype=packed.dtype, device=packed.device)
+    # flat [world * B, ...] output: the layout every backend accepts
+    buf = torch.empty((world * packed.shape[0], *packed.shape[1:]), dtype=packed.dtype,
+                      device=packed.device)
     dist.all_gather_into_tensor(buf, packed, group=group)
-    return unpack_states(buf)
+    return unpack_states(buf.view(world, *packed.shape))
 
 
 def sequence_sharded_decode(q: torch.Tensor, k_local: torch.Tensor, v_local: torch.Tensor,
