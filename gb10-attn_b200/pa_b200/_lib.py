@@ -45,6 +45,8 @@ SIGNATURES = {
                                       ctypes.POINTER(_SZ)]),
     "pa_paged_attention_v3": (_I, [_P, _P, _P, _P, _P, _I, _P, _P] + [_I64] * 7 +
                               [_D, _I64, _P, _SZ, _P, _P]),
+    "pa_paged_attention_v3_noalloc": (_I, [_P, _P, _P, _P, _P, _I, _P, _P] + [_I64] * 7 +
+                                      [_D, _I64, _P, _P]),
     "pa_paged_attention": (_I, [_P, _P, _P, _P, _I, _P, _P] + [_I64] * 7 +
                            [_D, _P, _SZ, _P, _P]),
     "pa_paged_attention_v2": (_I, [_P, _P, _P, _P, _I, _P, _P] + [_I64] * 7 +

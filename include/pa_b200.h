@@ -158,6 +158,28 @@ PA_API int pa_paged_attention_v2(float* out, const float* q, const void* k_cache
                           size_t workspace_bytes, int32_t* dev_status,
                           void* stream);
 
+/* pa_paged_attention_v3 for callers that cannot allocate device memory when
+ * they decode -- FFI hosts that only receive device pointers from elsewhere
+ * and have no allocator of their own, or serving loops that reserve all device
+ * memory up front.  No counterpart in the reference (its v3 allocates its
+ * scratch with torch::empty on every call).  Same arguments as
+ * pa_paged_attention_v3 minus the workspace: the scratch is an 8 MiB array
+ * inside the library (PA_NOALLOC_SCRATCH_BYTES, held on every GPU that loads
+ * the library until exit); sizes whose pa_decode_workspace_size exceeds it
+ * return PA_ERR_TOO_LARGE without launching.  The first call on a device
+ * looks up the array's device address (cudaGetSymbolAddress) with that device
+ * current; make that first call before any stream capture.  All calls on a
+ * device share the array, so calls that overlap on the GPU race: order them.
+ * Calls no cudaMalloc / cudaFree and no allocating library routine. */
+#define PA_NOALLOC_SCRATCH_BYTES (8u << 20)
+PA_API int pa_paged_attention_v3_noalloc(
+    float* out, float* lse, const float* q, const void* k_cache,
+    const void* v_cache, int kv_dtype, const int32_t* block_tables,
+    const int32_t* context_lens, int64_t num_seqs, int64_t num_heads,
+    int64_t num_kv_heads, int64_t head_dim, int64_t block_size,
+    int64_t num_blocks, int64_t max_blocks, double scale, int64_t num_splits,
+    int32_t* dev_status, void* stream);
+
 /* Merge per-device partial results of one decode (sequence-sharded
  * long-context decode): out[b,h,:] = sum_r w_r out_r[b,h,:] / sum_r w_r with
  * w_r = exp(lse_r[b,h] - max_r lse_r[b,h]); the log-sum-exp rule of
