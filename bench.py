@@ -282,6 +282,11 @@ def run_b200(args) -> None:
                      "isolated_launch_us": round(launch_ms * 1e3, 2)},
         "clocks": clk,
     }
+    if world == 1 and not args.no_extra:
+        del pools, outs
+        torch.cuda.empty_cache()
+        line["extra"] = {"config3_gqa_long_context": run_config3(torch, ops, harness, dev,
+                                                                 stream, args, peaks)}
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_baseline(args.cpu_seconds)
     if world > 1:
@@ -289,6 +294,66 @@ def run_b200(args) -> None:
         dist.destroy_process_group()
     if rank == 0:
         print(json.dumps(line), flush=True)
+
+
+def run_config3(torch, ops, harness, dev, stream, args, peaks) -> dict:
+    """bf16 GQA long-context decode, 32 query / 8 KV
+    heads, D=128, block_size 16, B=8, ctx ~ U[1024, 32768] (seeded), one K and
+    one V tensor of [140000, 16, 8, 128] = 2.29e9 elements each (> 2^31), the
+    blocks used drawn from the top of the pool so every offset crosses 2^31.
+    4 disjoint regions rotated per call (each call reads ~0.55 GB)."""
+    H3, HKV3, D3, BS3, B3, NB3, REG = 32, 8, 128, 16, 8, args.pool_blocks, 4
+    rng = np.random.default_rng(2026)
+    ctx = rng.integers(1024, 32769, size=B3).astype(np.int32)
+    need = [int(-(-c // BS3)) for c in ctx]
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(99)
+    kv = torch.empty((2, NB3, BS3, HKV3, D3), dtype=torch.bfloat16, device=dev)
+    kv.normal_(generator=gen)
+    top = NB3 - REG * sum(need)          # regions live in the top of the pool
+    tables = [t + top for t in harness.cold_regions(need, REG, REG * sum(need), seed=7)]
+    bt = [torch.from_numpy(t.astype(np.int32)).to(dev) for t in tables]
+    ctx_d = torch.from_numpy(ctx).to(dev)
+    q = torch.randn((B3, H3, D3), generator=gen, device=dev)
+    scale = D3 ** -0.5
+
+    def call(i):
+        return ops.paged_attention_v3(q, kv[0], kv[1], bt[i % REG], ctx_d, scale, 0)
+
+    # gate: two sequences against a dense fp32 reference
+    got = call(0)
+    err = 0.0
+    for b in (0, B3 - 1):
+        blocks = torch.from_numpy(tables[0][b, :need[b]].astype(np.int64)).to(dev)
+        kk = kv[0][blocks].float().reshape(-1, HKV3, D3)[:ctx[b]]
+        vv = kv[1][blocks].float().reshape(-1, HKV3, D3)[:ctx[b]]
+        kk = kk.repeat_interleave(H3 // HKV3, dim=1)
+        vv = vv.repeat_interleave(H3 // HKV3, dim=1)
+        sc = torch.einsum("hd,thd->ht", q[b], kk) * scale
+        want = torch.einsum("ht,thd->hd", torch.softmax(sc, -1), vv)
+        err = max(err, float((got[b] - want).abs().max()))
+        del kk, vv
+    for i in range(args.warmup):
+        call(i)
+    torch.cuda.synchronize()
+    n = max(50, args.steps)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for i in range(n):
+        call(i)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / n
+    per_call = harness.decode_bytes(ctx, H3, HKV3, D3, 2, BS3)
+    gbs = per_call / (ms * 1e-3) / 1e9
+    del kv
+    torch.cuda.empty_cache()
+    return {"value": round(gbs, 1), "unit": "GB/s",
+            "pct_of_measured_hbm_peak": round(100 * gbs / peaks["hbm_gbs"], 1),
+            "us_per_call": round(ms * 1e3, 2), "bytes_per_call": per_call,
+            "calls": n, "context_lens": ctx.tolist(), "pool_elements_per_tensor": NB3 * BS3 * HKV3 * D3,
+            "tokens_per_s": round(B3 / (ms * 1e-3), 1), "correctness_gate_max_abs": err,
+            "kernel": "pa::decode::decode_kernel<__nv_bfloat16,128,4> (warp-specialised)"}
 
 
 def correctness_gate(torch, layer_call, pool, q, bt_np, bt_dev, ctx_dev, scale, dev) -> float:
@@ -378,6 +443,18 @@ def cpu_baseline(seconds: float) -> dict:
             "sample": sample}
 
 
+def run_config3_only(args) -> None:
+    """--workload config3: the GQA long-context decode alone (profiler target)."""
+    import torch
+
+    from pa_b200 import harness, ops
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    r = run_config3(torch, ops, harness, dev, torch.cuda.current_stream(), args, _peaks())
+    print(json.dumps({"metric": METRIC, "value": r["value"], "unit": "GB/s", "n_gpus": 1,
+                      "workload": "configs[2]", "detail": r}), flush=True)
+
+
 def run_reference(args) -> None:
     rank, _, world = _env_rank()
     if rank != 0:
@@ -418,11 +495,18 @@ def main() -> None:
     ap.add_argument("--layers", type=int, default=12, help="fewer layers: profiler captures only")
     ap.add_argument("--regions", type=int, default=4, help="cold block regions in rotation")
     ap.add_argument("--no-e2e", action="store_true", help="skip the host-buffer e2e leg")
+    ap.add_argument("--no-extra", action="store_true", help="skip the config-3 GQA measurement")
+    ap.add_argument("--workload", choices=["config2", "config3"], default="config2",
+                    help="config3 runs the GQA long-context decode alone (profiling)")
+    ap.add_argument("--pool-blocks", type=int, default=140_000,
+                    help="config-3 pool blocks (140000: each K/V tensor > 2^31 elements)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
     if args.impl == "reference":
         run_reference(args)
+    elif args.workload == "config3":
+        run_config3_only(args)
     else:
         run_b200(args)
 

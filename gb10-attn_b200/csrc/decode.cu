@@ -36,14 +36,16 @@ int decode_elems_per_lane(int dtype, int D) {
   return (ch / r) * vec;
 }
 // Host mirrors of decode::Limits and of the QC cap in decode::kernel_if_fits.
-static bool decode_ws(int dtype, int D, int QC) {
+// Returns the CTA kind (decode::CtaKind) of an instantiation.
+static int decode_kind(int dtype, int D, int QC) {
   const int s = QC * decode_elems_per_lane(dtype, D);
-  return s >= 16 || (dtype_size(dtype) >= 4 && s >= 8);
+  if (dtype_size(dtype) == 2) return s <= 8 ? 0 : (s <= 32 ? 1 : 2);
+  return s <= 4 ? 0 : (s <= 16 ? 1 : 2);
 }
 static int decode_qc_cap(int dtype) {
   return dtype_size(dtype) == 2 ? 64 : (dtype_size(dtype) == 4 ? 32 : 16);
 }
-int decode_max_warps(int dtype, int D, int QC) { return decode_ws(dtype, D, QC) ? 8 : 16; }
+int decode_max_warps(int dtype, int D, int QC) { return decode_kind(dtype, D, QC) == 2 ? 8 : 16; }
 
 namespace decode {
 
@@ -231,18 +233,32 @@ static int configure(const DecodeArgs& a, Config* c) {
   const int elt = dtype_size(a.dtype);
   const int QPK = (int)(a.H / a.HKV);
   const int epl = decode_elems_per_lane(a.dtype, (int)a.D);
-  int QC = 1;
-  for (int qc : {8, 4, 2})
-    if (QPK % qc == 0 && qc * epl <= decode_qc_cap(a.dtype)) { QC = qc; break; }
-  const int maxw = decode_max_warps(a.dtype, (int)a.D, QC);
-  int G = 1;
-  for (int g = (int)std::min<int64_t>(a.HKV, 64); g >= 1; --g) {
-    if (a.HKV % g) continue;
-    if (g * (QPK / QC) > maxw) continue;
-    if (2u * kTT * (uint32_t)(g * a.D * elt) > kStageCap) continue;
+  // Query heads per consumer warp: the largest group whose state fits (each
+  // KV row is then read from shared memory by the fewest warps).  Measured on
+  // config 3: 8 warps x 4 heads and 16 warps x 2 heads run at the same speed.
+  auto pick_g = [&](int qc) {
+    const int maxw = decode_max_warps(a.dtype, (int)a.D, qc);
+    for (int g = (int)std::min<int64_t>(a.HKV, 64); g >= 1; --g) {
+      if (a.HKV % g) continue;
+      if (g * (QPK / qc) > maxw) continue;
+      if (2u * kTT * (uint32_t)(g * a.D * elt) > kStageCap) continue;
+      return g;
+    }
+    return 0;
+  };
+  int QC = 1, G = 0, best_ns = -1;
+  for (int qc : {8, 4, 2, 1}) {
+    if (QPK % qc || qc * epl > decode_qc_cap(a.dtype)) continue;
+    const int g = pick_g(qc);
+    if (g == 0) continue;
+    best_ns = g * (QPK / qc);
+    QC = qc;
     G = g;
     break;
   }
+  (void)best_ns;
+  if (G == 0) return PA_ERR_TOO_LARGE;  // QPK / QC beyond one CTA
+  const int maxw = decode_max_warps(a.dtype, (int)a.D, QC);
   c->QC = QC;
   c->G = G;
   c->NS = G * (QPK / QC);
@@ -252,7 +268,10 @@ static int configure(const DecodeArgs& a, Config* c) {
   const uint32_t stage_bytes = 2u * kTT * c->row_bytes;
   c->nstage = (int)std::max<uint32_t>(2, std::min<uint32_t>(8, kRingBudget / stage_bytes));
   // must match decode::Limits
-  c->threads = decode_ws(a.dtype, (int)a.D, QC) ? 384 : (c->NS + 1) * 32;
+  {
+    const int kind = decode_kind(a.dtype, (int)a.D, QC);
+    c->threads = kind == 2 ? 384 : (kind == 1 ? 640 : (c->NS + 1) * 32);
+  }
   c->smem = (size_t)c->nstage * stage_bytes + (size_t)c->nstage * (16 + sizeof(StageHeader));
   c->kernel = decode_kernel_ptr(a.dtype, (int)a.D, QC);
   if (!c->kernel) return PA_ERR_HEAD_DIM;

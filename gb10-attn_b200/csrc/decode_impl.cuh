@@ -86,31 +86,36 @@ struct Geo {
   static_assert(D % VEC == 0 && CH % R == 0 && 32 % R == 0 && NRG <= kTT, "geometry");
 };
 
-// CTA shape of a (T, D, QC) instantiation.
-//  * Light state (q and acc, 2 * QC * EPL floats, <= 16): up to 16 consumer
-//    warps 0..NS-1 plus the producer warp NS; (NS + 1) * 32 threads.
-//  * Heavier state (GQA groups, or head_dim >= 128): warp-specialised
-//    warpgroups.  Warpgroup 0 is the producer (warp 0 issues copies, warps 1-3
-//    retire) and gives registers back with setmaxnreg.dec to kProdRegs;
-//    warpgroups 1-2 are 8 consumer warps that raise their budget to
-//    kConsRegs.  Launched with 384 threads x 168 registers (12 warps, 3 per
-//    SM sub-partition) = 64512; after the split 128 x 48 + 256 x 224 = 63488,
-//    inside the launch total as setmaxnreg.inc requires.
+// CTA shape of a (T, D, QC) instantiation, by the per-lane register state
+// S = QC * EPL floats of q (and as many of acc):
+//  * kLight (S <= 8, or <= 4 for 4/8-byte types): consumer warps 0..NS-1 (up
+//    to 16) plus the producer warp NS; (NS + 1) * 32 threads.
+//  * kWs16 (S <= 32): warp-specialised.  Warpgroup 0 is the producer (warp 0
+//    issues copies, warps 1-3 retire) and hands registers back with
+//    setmaxnreg.dec; warpgroups 1-4 are up to 16 consumer warps.  640 threads
+//    launched at 96 registers (20 warps, 5 per SM sub-partition) = 61440; after
+//    the split 128 x 40 + 512 x 104 = 58368.
+//  * kWs8 (larger S): warpgroup 0 producer, warpgroups 1-2 = 8 consumer warps.
+//    384 threads x 168 registers = 64512; after the split 128 x 48 + 256 x 224
+//    = 63488.
+// setmaxnreg.inc draws on the registers the CTA was launched with, so each
+// split stays inside its launch total (checked below).
+enum CtaKind { kLight = 0, kWs16 = 1, kWs8 = 2 };
+
 template <typename T, int D, int QC>
 struct Limits {
-  static constexpr bool WS =
-      (QC * Geo<T, D>::EPL >= 16) || (sizeof(T) >= 4 && QC * Geo<T, D>::EPL >= 8);
-  static constexpr int MAXW = WS ? 8 : 16;
-  static constexpr int THREADS = WS ? 384 : (MAXW + 1) * 32;
+  static constexpr int S = QC * Geo<T, D>::EPL;
+  static constexpr int KIND = (sizeof(T) == 2 ? (S <= 8 ? kLight : (S <= 32 ? kWs16 : kWs8))
+                                              : (S <= 4 ? kLight : (S <= 16 ? kWs16 : kWs8)));
+  static constexpr bool WS = KIND != kLight;
+  static constexpr int MAXW = KIND == kWs8 ? 8 : 16;
+  static constexpr int THREADS = KIND == kWs8 ? 384 : (KIND == kWs16 ? 640 : 544);
+  static constexpr int PROD_REGS = KIND == kWs8 ? 48 : 40;
+  static constexpr int CONS_REGS = KIND == kWs8 ? 224 : 104;
 };
-constexpr int kProdRegs = 48;
-constexpr int kConsRegs = 224;
-static_assert(128 * kProdRegs + 256 * kConsRegs <= 384 * 168, "register split exceeds launch");
+static_assert(128 * 48 + 256 * 224 <= 384 * 168, "kWs8 register split exceeds launch");
+static_assert(128 * 40 + 512 * 104 <= 640 * 96, "kWs16 register split exceeds launch");
 
-// First global tile of CTA c.  With at least as many tiles as CTAs the
-// ranges are floor(c * T / N) (never empty); with fewer, CTA c takes tile c and
-// the CTAs past T are empty -- so the CTAs holding any one sequence are always
-// consecutive AND non-empty, which the last-arriver merge count relies on.
 __host__ __device__ __forceinline__ int64_t cta_lo(int64_t c, int64_t T_all, int64_t N) {
   return T_all >= N ? c * T_all / N : (c < T_all ? c : T_all);
 }
@@ -158,10 +163,10 @@ __global__ void __launch_bounds__(Limits<T, D, QC>::THREADS, 1)
 
   if constexpr (WS) {
     if (warp < 4) {
-      asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kProdRegs));
+      asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(Limits<T, D, QC>::PROD_REGS));
       if (warp != 0) return;
     } else {
-      asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kConsRegs));
+      asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(Limits<T, D, QC>::CONS_REGS));
       if (warp - 4 >= NS) return;
     }
   }
