@@ -7,7 +7,9 @@
 // position ctx - Sq + s and attends to keys [0, ctx - Sq + s]; a query with no
 // key (ctx - Sq + s < 0) is written as zeros.
 //
-// CUDA-core path (every pool dtype): the split-KV decode kernel with one
+// Tensor-core path (prefill_tc.cu): fp16 / bf16 pools, head_dim 64 or 128,
+// block_size a multiple of 16.  CUDA-core path (every other case, and
+// pa_paged_attention_prefill_simt): the split-KV decode kernel with one
 // pseudo-sequence per query row (qlen = Sq): row b*Sq + s reads block table
 // row b and sees ctx - Sq + s + 1 keys.  The balanced tile scheduler spreads
 // the triangular work evenly over the SMs.
@@ -15,6 +17,13 @@
 #include "common.cuh"
 
 namespace pa {
+namespace prefill {
+bool tc_eligible(int dtype, int64_t D, int64_t BS, int64_t NB);
+int launch_tc(float* out, const float* q, const void* k, const void* v, int dtype,
+              const int32_t* bt, const int32_t* ctx, int64_t B, int64_t Sq, int64_t H,
+              int64_t HKV, int64_t D, int64_t BS, int64_t NB, int64_t MB, double scale,
+              int32_t* dev_status, cudaStream_t s);
+}  // namespace prefill
 
 static int prefill_checks(int64_t B, int64_t Sq, int64_t H, int64_t HKV, int64_t D) {
   if (B < 0 || Sq < 0 || H <= 0 || HKV <= 0 || D <= 0) return PA_ERR_INVALID_ARGUMENT;
@@ -96,6 +105,14 @@ extern "C" int pa_paged_attention_prefill(float* out, const float* q, const void
                                           int64_t max_blocks, double scale, void* workspace,
                                           size_t workspace_bytes, int32_t* dev_status,
                                           void* stream) {
+  int st = pa::prefill_checks(num_seqs, num_queries, num_heads, num_kv_heads, head_dim);
+  if (st) return st;
+  if (num_seqs == 0 || num_queries == 0) return PA_OK;
+  if (pa::prefill::tc_eligible(kv_dtype, head_dim, block_size, num_blocks))
+    return pa::prefill::launch_tc(out, q, k_cache, v_cache, kv_dtype, block_tables, context_lens,
+                                  num_seqs, num_queries, num_heads, num_kv_heads, head_dim,
+                                  block_size, num_blocks, max_blocks, scale, dev_status,
+                                  static_cast<cudaStream_t>(stream));
   return pa_paged_attention_prefill_simt(out, q, k_cache, v_cache, kv_dtype, block_tables,
                                          context_lens, num_seqs, num_queries, num_heads,
                                          num_kv_heads, head_dim, block_size, num_blocks,
@@ -116,7 +133,7 @@ extern "C" int pa_paged_attention_prefill_wmma(
   if (num_heads % num_kv_heads != 0) return PA_ERR_NUM_HEADS;
   if (head_dim % 16 != 0 || (head_dim != 32 && head_dim != 64 && head_dim != 128))
     return PA_ERR_HEAD_DIM;
-  return pa_paged_attention_prefill_simt(out, q, k_cache, v_cache, kv_dtype, block_tables,
+  return pa_paged_attention_prefill(out, q, k_cache, v_cache, kv_dtype, block_tables,
                                          context_lens, num_seqs, num_queries, num_heads,
                                          num_kv_heads, head_dim, block_size, num_blocks,
                                          max_blocks, scale, workspace, workspace_bytes,

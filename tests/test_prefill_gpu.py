@@ -66,3 +66,25 @@ def test_shim_prefill_and_wmma_checks():
         ops.paged_attention_prefill_wmma(args[0], k8, k8, *args[3:], 0.125)
     with pytest.raises(RuntimeError, match=r"q must be \[B, S, H, D\]"):
         ops.paged_attention_prefill(args[0][0], *args[1:], 0.125)
+
+
+@pytest.mark.parametrize("dtype,D", [("bfloat16", 128), ("float16", 128), ("bfloat16", 64),
+                                     ("float16", 64)])
+def test_tensor_core_path_multi_tile_gqa(dtype, D):
+    # 3 query tiles of 128 rows, a 700-token context (ragged last page and
+    # last KV tile), GQA 8q/2kv: the tcgen05 path against oracle and SIMT path
+    q, k, v, bt, ctx = case(44, 2, 300, 8, 2, D, 16, [700, 300], dtype)
+    scale = D ** -0.5
+    ref = orc.prefill(q, k, v, bt, ctx, scale, threads=8)
+    tc = abi_prefill(q, k, v, bt, ctx, scale, dtype)
+    simt = abi_prefill(q, k, v, bt, ctx, scale, dtype, entry="pa_paged_attention_prefill_simt")
+    assert max_abs(tc, ref) <= 2e-3
+    assert max_abs(simt, ref) <= 2e-3
+
+
+def test_tensor_core_path_block_size_32_and_padding():
+    # block_size 32 (two 16-row boxes per page); Sq > ctx for seq 0 (padded rows)
+    q, k, v, bt, ctx = case(45, 2, 150, 4, 4, 128, 32, [100, 400], "bfloat16")
+    out = abi_prefill(q, k, v, bt, ctx, 0.088, "bfloat16")
+    assert np.all(out[0, :50] == 0)
+    assert max_abs(out, orc.prefill(q, k, v, bt, ctx, 0.088, threads=8)) <= 2e-3
