@@ -286,7 +286,8 @@ def run_b200(args) -> None:
         del pools, outs
         torch.cuda.empty_cache()
         line["extra"] = {"config3_gqa_long_context": run_config3(torch, ops, harness, dev,
-                                                                 stream, args, peaks)}
+                                                                 stream, args, peaks),
+                         "config4_prefill": run_config4(torch, ops, harness, dev, stream, args)}
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_baseline(args.cpu_seconds)
     if world > 1:
@@ -443,6 +444,95 @@ def cpu_baseline(seconds: float) -> dict:
             "sample": sample}
 
 
+def run_config4(torch, ops, harness, dev, stream, args) -> dict:
+    """bf16 causal prefill, B=4, Sq = ctx = 4096,
+    32 heads (MHA), D=128, block_size 16, K/V written into the paged pool by
+    write_kv (timed too), q fp32 per the reference signature.  Tensor roofline:
+    algorithmic flops 4*D per (query, visible key) per head."""
+    from pa_b200.kv import KVConfig, ModelConfig, TorchBlockAllocator
+    B4, S4, H4, D4, BS4 = 4, 4096, 32, 128, 16
+    alloc = TorchBlockAllocator(KVConfig(BS4, B4 * S4 // BS4 + 8, "bfloat16"),
+                                ModelConfig(n_layer=1, n_head=H4, head_dim=D4), dev)
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(4)
+    allocs = [alloc.allocate(range(S4)) for _ in range(B4)]
+    ks = [torch.randn((1, H4, S4, D4), generator=gen, device=dev) for _ in range(B4)]
+    vs = [torch.randn((1, H4, S4, D4), generator=gen, device=dev) for _ in range(B4)]
+    torch.cuda.synchronize()
+    w0, w1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    w0.record(stream)
+    for a, kk, vv in zip(allocs, ks, vs):
+        alloc.write_kv(a.block_ids, 0, kk, vv)
+    w1.record(stream)
+    torch.cuda.synchronize()
+    wkv_ms = w0.elapsed_time(w1)
+    wkv_bytes = B4 * 2 * H4 * S4 * D4 * (4 + 2)  # fp32 read + bf16 write
+    kc, vc = alloc.layer_kv(0)
+    bt = alloc.block_table(allocs)
+    ctx = torch.full((B4,), S4, dtype=torch.int32, device=dev)
+    q = torch.randn((B4, S4, H4, D4), generator=gen, device=dev)
+    scale = D4 ** -0.5
+
+    def call():
+        return ops.paged_attention_prefill(q, kc, vc, bt, ctx, scale)
+
+    out = call()
+    # gate: sequence 0, head 0, all 4096 rows, dense fp32 causal reference
+    kk = ks[0][0, 0].to(torch.bfloat16).float()
+    vv = vs[0][0, 0].to(torch.bfloat16).float()
+    sc = (q[0, :, 0] @ kk.T) * scale
+    sc = sc.masked_fill(torch.triu(torch.ones(S4, S4, dtype=torch.bool, device=dev), 1),
+                        float("-inf"))
+    want = torch.softmax(sc, -1) @ vv
+    err = float((out[0, :, 0] - want).abs().max())
+    del kk, vv, sc, want, ks, vs
+    for _ in range(args.warmup):
+        call()
+    torch.cuda.synchronize()
+    n = max(10, args.steps // 10)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(n):
+        call()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / n
+    flops = harness.prefill_flops([S4] * B4, S4, H4, D4)
+    tflops = flops / (ms * 1e-3) / 1e12
+    peak = _peak_tflops()
+    return {"value": round(tflops, 1), "unit": "TFLOP/s",
+            "pct_of_measured_bf16_peak": round(100 * tflops / peak["bf16_tflops"], 1),
+            "peak_source": peak["src"], "ms_per_call": round(ms, 4), "flops_per_call": flops,
+            "calls": n, "correctness_gate_max_abs": err,
+            "kernel": "pa::prefill::prefill_tc_kernel<__nv_bfloat16,128> (tcgen05, bf16 hi/lo)",
+            "write_kv": {"value": round(wkv_bytes / (wkv_ms * 1e-3) / 1e9, 1), "unit": "GB/s",
+                         "bytes": wkv_bytes, "ms": round(wkv_ms, 3),
+                         "note": "4 sequences x 4096 tokens x 32 heads, fp32 device source"}}
+
+
+def _peak_tflops() -> dict:
+    p = REPO / "MEASURED_PEAKS.json"
+    if p.exists():
+        try:
+            d = json.loads(p.read_text())
+            return {"bf16_tflops": float(d["bf16_tflops"]), "src": "measured (burst)"}
+        except (OSError, ValueError, KeyError):
+            pass
+    return {"bf16_tflops": 1590.0, "src": "fallback"}
+
+
+def run_config4_only(args) -> None:
+    """--workload config4: the causal prefill alone (profiling)."""
+    import torch
+
+    from pa_b200 import harness, ops
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    r = run_config4(torch, ops, harness, dev, torch.cuda.current_stream(), args)
+    print(json.dumps({"metric": "causal prefill TFLOP/s", "value": r["value"], "unit": "TFLOP/s",
+                      "n_gpus": 1, "workload": "configs[3]", "detail": r}), flush=True)
+
+
 def run_config3_only(args) -> None:
     """--workload config3: the GQA long-context decode alone (profiler target)."""
     import torch
@@ -496,8 +586,8 @@ def main() -> None:
     ap.add_argument("--regions", type=int, default=4, help="cold block regions in rotation")
     ap.add_argument("--no-e2e", action="store_true", help="skip the host-buffer e2e leg")
     ap.add_argument("--no-extra", action="store_true", help="skip the config-3 GQA measurement")
-    ap.add_argument("--workload", choices=["config2", "config3"], default="config2",
-                    help="config3 runs the GQA long-context decode alone (profiling)")
+    ap.add_argument("--workload", choices=["config2", "config3", "config4"], default="config2",
+                    help="config3 / config4 run the GQA decode / the prefill alone (profiling)")
     ap.add_argument("--pool-blocks", type=int, default=140_000,
                     help="config-3 pool blocks (140000: each K/V tensor > 2^31 elements)")
     args = ap.parse_args()
@@ -507,6 +597,8 @@ def main() -> None:
         run_reference(args)
     elif args.workload == "config3":
         run_config3_only(args)
+    elif args.workload == "config4":
+        run_config4_only(args)
     else:
         run_b200(args)
 

@@ -119,6 +119,22 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   return ok != 0;
 }
 
+// try_wait that lets the hardware suspend the thread (up to `hint_ns`) until
+// the phase completes, instead of returning at once: waiting warps then do
+// not take issue slots from the warps doing the work.
+__device__ __forceinline__ bool mbar_try_wait_sleep(uint64_t* bar, uint32_t parity,
+                                                    uint32_t hint_ns) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.acquire.cta.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity), "r"(hint_ns)
+      : "memory");
+  return ok != 0;
+}
+
 __device__ __forceinline__ uint64_t globaltimer_ns() {
   uint64_t t;
   asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
@@ -137,8 +153,8 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity,
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = globaltimer_ns();
   for (uint32_t it = 1;; ++it) {
-    if (mbar_try_wait(bar, parity)) return true;
-    if ((it & 63) == 0) {
+    if (mbar_try_wait_sleep(bar, parity, 100000u)) return true;
+    if ((it & 7) == 0) {
       if (abort_flag && *reinterpret_cast<volatile int32_t*>(abort_flag) != 0) return false;
       if (globaltimer_ns() - t0 > kWaitLimitNs) {
         if (abort_flag) atomicExch(abort_flag, 1);

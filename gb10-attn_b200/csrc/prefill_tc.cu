@@ -43,7 +43,10 @@ namespace prefill {
 
 constexpr int BM = 128;  // query rows per CTA
 constexpr int BN = 128;  // keys per KV tile
-constexpr int kThreads = 192;  // warps 0-3 softmax, warp 4 MMA, warp 5 TMA
+constexpr int kSoftmaxWarps = 8;  // two per TMEM lane quadrant
+constexpr int kMmaWarp = 8;
+constexpr int kTmaWarp = 9;
+constexpr int kThreads = 320;
 constexpr uint32_t kTmemCols = 512;
 
 struct Params {
@@ -70,14 +73,20 @@ struct Cfg {
   static constexpr int NH = D / 64;                 // 64-element (128-byte) column halves
   static constexpr uint32_t Q_BYTES = BM * D * 2;   // one Q part
   static constexpr uint32_t KV_BYTES = BN * D * 2;  // K or V of one tile
-  static constexpr int NST = D == 128 ? 2 : 4;      // K/V stages
+  // K stages are freed as soon as S = Q K^T is done, V stages after P V, so
+  // the K ring runs one tile deeper.
+  static constexpr int NK = D == 128 ? 3 : 4;
+  static constexpr int NV = D == 128 ? 2 : 4;
   static constexpr uint32_t OFF_QH = 0;
   static constexpr uint32_t OFF_QL = Q_BYTES;
-  static constexpr uint32_t OFF_KV = Q_BYTES * (SPLIT ? 2 : 1);
-  static constexpr uint32_t OFF_BAR = OFF_KV + NST * 2 * KV_BYTES;
-  static constexpr uint32_t SMEM = OFF_BAR + 256 + 1024;  // + barriers + alignment slack
-  // TMEM columns: S buffers at 0 and 128, O at 256
-  static constexpr uint32_t COL_S0 = 0, COL_S1 = 128, COL_O = 256;
+  static constexpr uint32_t OFF_K = Q_BYTES * (SPLIT ? 2 : 1);
+  static constexpr uint32_t OFF_V = OFF_K + NK * KV_BYTES;
+  static constexpr uint32_t OFF_BAR = OFF_V + NV * KV_BYTES;
+  static constexpr uint32_t SMEM = OFF_BAR + 192 + 1024;  // + barriers + alignment slack
+  static_assert(SMEM <= 227 * 1024, "shared memory budget");
+  // TMEM columns: S buffers at 0 and 128, O at 256, row-max / sum exchange
+  // slots of the softmax warp pairs at 384..387
+  static constexpr uint32_t COL_S0 = 0, COL_S1 = 128, COL_O = 256, COL_X = 384;
 };
 
 __device__ __forceinline__ uint32_t pack2(float lo, float hi, __nv_bfloat16*) {
@@ -97,6 +106,23 @@ __device__ __forceinline__ float unpack_lo(uint32_t u, __half*) {
 }
 __device__ __forceinline__ float unpack_hi(uint32_t u, __half*) {
   return __half2float(__ushort_as_half((unsigned short)(u >> 16)));
+}
+
+// Two fp32 values -> packed 16-bit pair (first value in the low half).  For
+// bf16 also the remainder pair: hi = the fp32 bits truncated to bf16 (exact),
+// lo = round-to-nearest bf16 of the exact fp32 remainder x - hi, so hi + lo
+// carries x to ~2^-16 relative.  fp16: one round-to-nearest pair, lo unused.
+__device__ __forceinline__ void split_pair(float a, float b, uint32_t& hi, uint32_t& lo,
+                                           __nv_bfloat16*) {
+  const uint32_t ua = __float_as_uint(a), ub = __float_as_uint(b);
+  hi = __byte_perm(ua, ub, 0x7632);
+  const float ra = a - __uint_as_float(ua & 0xffff0000u);
+  const float rb = b - __uint_as_float(ub & 0xffff0000u);
+  lo = pack2(ra, rb, (__nv_bfloat16*)nullptr);
+}
+__device__ __forceinline__ void split_pair(float a, float b, uint32_t& hi, uint32_t& lo, __half*) {
+  hi = pack2(a, b, (__half*)nullptr);
+  lo = 0;
 }
 
 // Byte offset of element (r, k) of a [rows x D] K-major tile stored as D/64
@@ -122,46 +148,54 @@ __device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, int32_
 template <typename T, int D>
 __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const __grid_constant__ Params p) {
   using C = Cfg<T, D>;
-  constexpr int NST = C::NST;
+  constexpr int NK = C::NK, NV = C::NV;
   extern __shared__ unsigned char smem_raw[];
   // 1024-byte alignment for the 128-byte-swizzle atoms
   unsigned char* smem = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::OFF_BAR);
-  uint64_t* kv_full = bars;              // [NST] TMA landed
-  uint64_t* kv_empty = bars + NST;       // [NST] MMAs reading the stage done
-  uint64_t* s_full = bars + 2 * NST;     // [2] S tile in TMEM
-  uint64_t* p_full = s_full + 2;         // [2] P written to TMEM (4 warps)
+  uint64_t* k_full = bars;               // [NK] K tile landed
+  uint64_t* k_empty = k_full + NK;       // [NK] S = Q K^T done with it
+  uint64_t* v_full = k_empty + NK;       // [NV] V tile landed
+  uint64_t* v_empty = v_full + NV;       // [NV] P V done with it
+  uint64_t* s_full = v_empty + NV;       // [2] S tile in TMEM
+  uint64_t* p_full = s_full + 2;         // [2] P written to TMEM (softmax warps)
   uint64_t* o_ready = p_full + 2;        // PV of a tile done
-  uint64_t* q_ready = o_ready + 1;       // Q in shared memory (4 warps)
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(q_ready + 1);
+  uint64_t* q_ready = o_ready + 1;       // Q in shared memory (softmax warps)
+  uint64_t* pair_bar = q_ready + 1;     // [4] max / sum exchange of a warp pair (64 threads)
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(pair_bar + 4);
   int32_t* abort_s = reinterpret_cast<int32_t*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
-  // LPT order: the query tiles with the most keys first
-  const int64_t bh_count = p.B * p.H;
+  // Consecutive CTAs take the query tiles of one (sequence, head), longest
+  // first: the CTAs resident together share that head's K/V in L2.
   const int64_t c = blockIdx.x;
-  const int qt = p.n_qtiles - 1 - (int)(c / bh_count);
-  const int64_t bh = c % bh_count;
+  const int qt = p.n_qtiles - 1 - (int)(c % p.n_qtiles);
+  const int64_t bh = c / p.n_qtiles;
   const int64_t b = bh / p.H, h = bh % p.H;
   const int64_t kv_h = h / (p.H / p.HKV);
   const int64_t q0 = (int64_t)qt * BM;
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < NST; ++s) {
-      mbar_init(&kv_full[s], 1);
-      mbar_init(&kv_empty[s], 1);
+    for (int s = 0; s < NK; ++s) {
+      mbar_init(&k_full[s], 1);
+      mbar_init(&k_empty[s], 1);
+    }
+    for (int s = 0; s < NV; ++s) {
+      mbar_init(&v_full[s], 1);
+      mbar_init(&v_empty[s], 1);
     }
     for (int s = 0; s < 2; ++s) {
       mbar_init(&s_full[s], 1);
-      mbar_init(&p_full[s], 4);
+      mbar_init(&p_full[s], kSoftmaxWarps * 32);
     }
     mbar_init(o_ready, 1);
-    mbar_init(q_ready, 4);
+    mbar_init(q_ready, kSoftmaxWarps * 32);
+    for (int qd = 0; qd < 4; ++qd) mbar_init(&pair_bar[qd], 64);
     *abort_s = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
-  if (warp == 4) {
+  if (warp == kMmaWarp) {
     tc::tmem_alloc(tmem_slot, kTmemCols);
     tc::tmem_relinquish();
   }
@@ -181,19 +215,25 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const __grid_co
   const int64_t key_end = min(ctx, ctx - p.Sq + q_last + 1);
   const int n_tiles = key_end > 0 ? (int)((key_end + BN - 1) / BN) : 0;
 
-  if (warp < 4) {
+  if (warp < kSoftmaxWarps) {
     // ------------------------------------------------------------------ softmax
-    const int r = threadIdx.x;  // query row in the tile = TMEM lane
+    // Warp w serves query rows 32 * (w % 4) .. +31 (its TMEM lane quadrant) and
+    // key columns 64 * (w / 4) .. +63 of each S tile; the two warps of a
+    // quadrant share each row's max through shared memory.
+    const int quad = warp & 3, ch = warp >> 2;
+    const int r = quad * 32 + lane;  // query row in the tile = TMEM lane
     const int64_t qrow = q0 + r;
     const bool row_valid = qrow < p.Sq;
     const int64_t q_abs = ctx - p.Sq + qrow;  // absolute position of this query
-    // Q tile -> shared memory, pre-scaled, hi (+ lo) parts, swizzled.
+    // Q tile -> shared memory, pre-scaled, hi (+ lo) parts, swizzled: warp w
+    // converts rows 16w .. 16w+15.
     {
       unsigned char* qh = smem + C::OFF_QH;
       unsigned char* ql = smem + C::OFF_QL;
       constexpr int EPT = D / 32;  // elements per lane per row
-      for (int i = 0; i < 32; ++i) {
-        const int rr = warp * 32 + i;
+#pragma unroll
+      for (int i = 0; i < BM / kSoftmaxWarps; ++i) {
+        const int rr = warp * (BM / kSoftmaxWarps) + i;
         const int64_t qr = q0 + rr;
         float x[EPT];
         if (qr < p.Sq) {
@@ -210,64 +250,76 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const __grid_co
         }
 #pragma unroll
         for (int e = 0; e < EPT; e += 2) {
-          const uint32_t hi = pack2(x[e], x[e + 1], (T*)nullptr);
           const uint32_t off = sw128_offset(rr, lane * EPT + e, BM);
+          uint32_t hi, lo;
+          split_pair(x[e], x[e + 1], hi, lo, (T*)nullptr);
           *reinterpret_cast<uint32_t*>(qh + off) = hi;
-          if constexpr (C::SPLIT) {
-            const float r0 = x[e] - unpack_lo(hi, (T*)nullptr);
-            const float r1 = x[e + 1] - unpack_hi(hi, (T*)nullptr);
-            *reinterpret_cast<uint32_t*>(ql + off) = pack2(r0, r1, (T*)nullptr);
-          }
+          if constexpr (C::SPLIT) *reinterpret_cast<uint32_t*>(ql + off) = lo;
         }
       }
       tc::fence_proxy_async_smem();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(q_ready);
+      mbar_arrive(q_ready);
     }
 
-    const uint32_t lane_base = tmem + ((uint32_t)(warp * 32) << 16);
+    constexpr int HC = BN / 2;  // key columns per warp
+    const uint32_t lane_base = tmem + ((uint32_t)(quad * 32) << 16);
     float m_ref = -INFINITY, l = 0.f;
     bool ok = true;
     for (int j = 0; j < n_tiles && ok; ++j) {
       if (!warp_wait(&s_full[j & 1], (j >> 1) & 1, abort_s)) { ok = false; break; }
       tc::fence_after_sync();
-      const uint32_t scol = (j & 1) ? C::COL_S1 : C::COL_S0;
-      float s[BN];
+      const uint32_t scol = ((j & 1) ? C::COL_S1 : C::COL_S0);
+      float s[HC];
 #pragma unroll
-      for (int c4 = 0; c4 < BN / 32; ++c4) {
+      for (int c4 = 0; c4 < HC / 32; ++c4) {
         uint32_t u[32];
-        tc::tmem_ld32(lane_base + scol + 32 * c4, u);
+        tc::tmem_ld32(lane_base + scol + ch * HC + 32 * c4, u);
         tc::tmem_wait_ld();
 #pragma unroll
         for (int i = 0; i < 32; ++i) s[32 * c4 + i] = __uint_as_float(u[i]);
       }
-      // causal rule + context bound (kernels/paged_attn_prefill.cu:62-65)
-      const int64_t k0 = (int64_t)j * BN;
-      int64_t lim = min(q_abs + 1, ctx) - k0;  // keys [k0, k0 + lim) are visible
-      if (!row_valid) lim = 0;
+      // causal rule + context bound (kernels/paged_attn_prefill.cu:62-65):
+      // this warp's keys k0 + c, c < HC, are visible when c < lim
+      const int64_t k0 = (int64_t)j * BN + ch * HC;
+      const int64_t vis = row_valid ? min(q_abs + 1, ctx) - k0 : 0;
+      const int lim = vis <= 0 ? 0 : (vis >= HC ? HC : (int)vis);
       float mt = -INFINITY;
 #pragma unroll
-      for (int i = 0; i < BN; ++i) {
-        if (i >= lim) s[i] = -INFINITY;
+      for (int i = 0; i < HC; ++i) {
+        s[i] = (i < lim) ? s[i] : -INFINITY;
         mt = fmaxf(mt, s[i]);
+      }
+      // row max over both column halves, exchanged through TMEM slot j & 1 (a
+      // warp is at most one tile ahead of its partner, so the slots alternate)
+      tc::tmem_st1(lane_base + C::COL_X + 2 * (j & 1) + ch, __float_as_uint(mt));
+      tc::tmem_wait_st();
+      tc::fence_before_sync();
+      mbar_arrive(&pair_bar[quad]);
+      if (!warp_wait(&pair_bar[quad], j & 1, abort_s)) { ok = false; break; }
+      tc::fence_after_sync();
+      {
+        const uint32_t other = tc::tmem_ld1(lane_base + C::COL_X + 2 * (j & 1) + (ch ^ 1));
+        tc::tmem_wait_ld();
+        mt = fmaxf(mt, __uint_as_float(other));
       }
       // The reference max of a row moves only when the row's max grows by more
       // than 2^8 (then O and l are rescaled); the O rescale is done by the
-      // whole warp (tcgen05.ld/st are warp-collective), factor 1 for rows
-      // that keep their reference.
+      // whole warp (tcgen05.ld/st are warp-collective) on its half of O's
+      // columns, factor 1 for rows that keep their reference.
       const bool need = mt > m_ref + 8.f;
       const float factor = need ? fast_exp2(m_ref - mt) : 1.f;  // 0 on a row's first visible tile
-      if (__any_sync(0xffffffffu, need && j > 0 && l > 0.f)) {
+      if (__any_sync(0xffffffffu, need) && j > 0) {
         if (!warp_wait(o_ready, (j - 1) & 1, abort_s)) { ok = false; break; }
         tc::fence_after_sync();
 #pragma unroll
-        for (int c4 = 0; c4 < D / 32; ++c4) {
+        for (int c4 = 0; c4 < D / 64; ++c4) {
           uint32_t u[32];
-          tc::tmem_ld32(lane_base + C::COL_O + 32 * c4, u);
+          const uint32_t col = lane_base + C::COL_O + ch * (D / 2) + 32 * c4;
+          tc::tmem_ld32(col, u);
           tc::tmem_wait_ld();
 #pragma unroll
           for (int i = 0; i < 32; ++i) u[i] = __float_as_uint(__uint_as_float(u[i]) * factor);
-          tc::tmem_st32(lane_base + C::COL_O + 32 * c4, u);
+          tc::tmem_st32(col, u);
         }
         tc::tmem_wait_st();
       }
@@ -277,7 +329,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const __grid_co
       }
       float lsum = 0.f;
 #pragma unroll
-      for (int i = 0; i < BN; ++i) {
+      for (int i = 0; i < HC; ++i) {
         const float e = (i < lim) ? fast_exp2(s[i] - m_ref) : 0.f;
         s[i] = e;
         lsum += e;
@@ -285,73 +337,81 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const __grid_co
       l += lsum;
       // Keys of this tile past the context (tail of the last page) get P = 0,
       // but 0 * NaN is NaN: zero their V rows in the stage before P V runs
-      // (an unwritten pool row may hold anything).  Thread r owns V row r.
-      if (k0 + BN > ctx && r >= ctx - k0) {
-        unsigned char* vrow = smem + C::OFF_KV + (j % NST) * 2 * C::KV_BYTES + C::KV_BYTES +
-                              (r >> 3) * 1024 + (r & 7) * 128;
+      // (an unwritten pool row may hold anything).  The warp pair of quadrant
+      // q zeroes rows 32q .. 32q+31, each warp half of every row.
+      {
+        const int64_t vr = (int64_t)j * BN + r;
+        if (vr >= ctx) {
+          unsigned char* vrow = smem + C::OFF_V + (j % NV) * C::KV_BYTES +
+                                (r >> 3) * 1024 + (r & 7) * 128;
 #pragma unroll
-        for (int hf = 0; hf < C::NH; ++hf)
+          for (int hf = 0; hf < C::NH; ++hf)
 #pragma unroll
-          for (int c16 = 0; c16 < 8; ++c16)
-            *reinterpret_cast<uint4*>(vrow + hf * (BN * 128) + c16 * 16) = make_uint4(0, 0, 0, 0);
-        tc::fence_proxy_async_smem();
-      }
-      // P (hi, lo) into the S columns: column c holds keys 2c (low half), 2c+1
-#pragma unroll
-      for (int part = 0; part < (C::SPLIT ? 2 : 1); ++part) {
-#pragma unroll
-        for (int c2 = 0; c2 < BN / 64; ++c2) {
-          uint32_t u[32];
-#pragma unroll
-          for (int i = 0; i < 32; ++i) {
-            const float a = s[64 * c2 + 2 * i], bb = s[64 * c2 + 2 * i + 1];
-            const uint32_t hi = pack2(a, bb, (T*)nullptr);
-            if (part == 0) {
-              u[i] = hi;
-            } else {
-              u[i] = pack2(a - unpack_lo(hi, (T*)nullptr), bb - unpack_hi(hi, (T*)nullptr),
-                           (T*)nullptr);
-            }
-          }
-          tc::tmem_st32(lane_base + scol + part * (BN / 2) + 32 * c2, u);
+            for (int c16 = ch * 4; c16 < ch * 4 + 4; ++c16)
+              *reinterpret_cast<uint4*>(vrow + hf * (BN * 128) + c16 * 16) = make_uint4(0, 0, 0, 0);
+          tc::fence_proxy_async_smem();
         }
+      }
+      // P into the S columns: column c of the S buffer holds keys 2c (low half)
+      // and 2c+1; P hi in columns [0, 64), P lo in [64, 128).
+      {
+        uint32_t uh[32], ul[32];
+#pragma unroll
+        for (int i = 0; i < 32; ++i) split_pair(s[2 * i], s[2 * i + 1], uh[i], ul[i], (T*)nullptr);
+        tc::tmem_st32(lane_base + scol + ch * 32, uh);
+        if constexpr (C::SPLIT) tc::tmem_st32(lane_base + scol + BN / 2 + ch * 32, ul);
       }
       tc::tmem_wait_st();
       tc::fence_before_sync();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&p_full[j & 1]);
+      mbar_arrive(&p_full[j & 1]);
     }
 
-    // epilogue: O / l -> out
-    float o[D];
+    // epilogue: O / l -> out (this warp's half of the columns); the pair's
+    // partial sums meet through slot n_tiles & 1 (phase n_tiles of pair_bar)
+    if (ok) {
+      tc::tmem_st1(lane_base + C::COL_X + 2 * (n_tiles & 1) + ch, __float_as_uint(l));
+      tc::tmem_wait_st();
+      tc::fence_before_sync();
+      mbar_arrive(&pair_bar[quad]);
+      if (warp_wait(&pair_bar[quad], n_tiles & 1, abort_s)) {
+        tc::fence_after_sync();
+        const uint32_t other = tc::tmem_ld1(lane_base + C::COL_X + 2 * (n_tiles & 1) + (ch ^ 1));
+        tc::tmem_wait_ld();
+        l += __uint_as_float(other);
+      } else {
+        ok = false;
+      }
+    }
+    constexpr int HD = D / 2;
+    float o[HD];
 #pragma unroll
-    for (int i = 0; i < D; ++i) o[i] = 0.f;
+    for (int i = 0; i < HD; ++i) o[i] = 0.f;
     if (ok && n_tiles > 0) {
       if (warp_wait(o_ready, (n_tiles - 1) & 1, abort_s)) {
         tc::fence_after_sync();
 #pragma unroll
-        for (int c4 = 0; c4 < D / 32; ++c4) {
+        for (int c4 = 0; c4 < HD / 32; ++c4) {
           uint32_t u[32];
-          tc::tmem_ld32(lane_base + C::COL_O + 32 * c4, u);
+          tc::tmem_ld32(lane_base + C::COL_O + ch * HD + 32 * c4, u);
           tc::tmem_wait_ld();
 #pragma unroll
           for (int i = 0; i < 32; ++i) o[32 * c4 + i] = __uint_as_float(u[i]);
         }
         const float inv = l > 0.f ? 1.f / l : 0.f;
 #pragma unroll
-        for (int i = 0; i < D; ++i) o[i] *= inv;
+        for (int i = 0; i < HD; ++i) o[i] *= inv;
       } else {
         ok = false;
       }
     }
     if (row_valid) {
-      float* dst = p.out + ((b * p.Sq + qrow) * p.H + h) * D;
+      float* dst = p.out + ((b * p.Sq + qrow) * p.H + h) * D + ch * HD;
 #pragma unroll
-      for (int i = 0; i < D; i += 4)
+      for (int i = 0; i < HD; i += 4)
         *reinterpret_cast<float4*>(dst + i) = make_float4(o[i], o[i + 1], o[i + 2], o[i + 3]);
     }
     if (!ok && lane == 0) report(p.dev_status, PA_DEVERR_TIMEOUT);
-  } else if (warp == 4) {
+  } else if (warp == kMmaWarp) {
     // ------------------------------------------------------------- MMA issuer
     if (lane == 0 && n_tiles > 0) {
       constexpr uint32_t idesc_s = tc::idesc_f16(Fmt<T>::id, BM, BN, false);
@@ -360,10 +420,10 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const __grid_co
       bool ok = mbar_wait(q_ready, 0, abort_s);
       tc::fence_after_sync();
       auto issue_s = [&](int jj) -> bool {
-        const int st = jj % NST;
-        if (!mbar_wait(&kv_full[st], (jj / NST) & 1, abort_s)) return false;
+        const int st = jj % NK;
+        if (!mbar_wait(&k_full[st], (jj / NK) & 1, abort_s)) return false;
         tc::fence_after_sync();
-        const uint32_t kb = smem_u32(smem + C::OFF_KV + st * 2 * C::KV_BYTES);
+        const uint32_t kb = smem_u32(smem + C::OFF_K + st * C::KV_BYTES);
         const uint32_t dcol = tmem + ((jj & 1) ? C::COL_S1 : C::COL_S0);
 #pragma unroll
         for (int part = 0; part < (C::SPLIT ? 2 : 1); ++part) {
@@ -377,15 +437,17 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const __grid_co
           }
         }
         tc::mma_commit(&s_full[jj & 1]);
+        tc::mma_commit(&k_empty[st]);
         return true;
       };
       if (ok) ok = issue_s(0);
       for (int j = 0; j < n_tiles && ok; ++j) {
         if (j + 1 < n_tiles && !issue_s(j + 1)) { ok = false; break; }
         if (!mbar_wait(&p_full[j & 1], (j >> 1) & 1, abort_s)) { ok = false; break; }
+        const int vs = j % NV;
+        if (!mbar_wait(&v_full[vs], (j / NV) & 1, abort_s)) { ok = false; break; }
         tc::fence_after_sync();
-        const int st = j % NST;
-        const uint32_t vb = smem_u32(smem + C::OFF_KV + st * 2 * C::KV_BYTES + C::KV_BYTES);
+        const uint32_t vb = smem_u32(smem + C::OFF_V + vs * C::KV_BYTES);
         const uint32_t pcol = tmem + ((j & 1) ? C::COL_S1 : C::COL_S0);
 #pragma unroll
         for (int part = 0; part < (C::SPLIT ? 2 : 1); ++part) {
@@ -396,46 +458,63 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const __grid_co
                        (j > 0 || part > 0 || kk > 0) ? 1u : 0u);
           }
         }
-        tc::mma_commit(&kv_empty[st]);
+        tc::mma_commit(&v_empty[vs]);
         tc::mma_commit(o_ready);
       }
       if (!ok) report(p.dev_status, PA_DEVERR_TIMEOUT);
     }
-  } else {
+  } else if (warp == kTmaWarp) {
     // ------------------------------------------------------------- TMA producer
-    constexpr int NBOX = 8 * C::NH * 2;  // 16-row groups x column halves x {K, V}
-    const int kv = lane / (NBOX / 2);
-    const int g16 = (lane % (NBOX / 2)) / C::NH;
+    // Lane l < 8 * NH loads one 16-row group x 64-column half of the K tile
+    // (then of the V tile); the K tile of j runs up to NK tiles ahead, the V
+    // tile up to NV.  Block ids are read one tile ahead of their use.
+    constexpr int NBOX = 8 * C::NH;
+    const int g16 = lane / C::NH;
     const int hf = lane % C::NH;
     const int32_t* bt = p.block_tables + b * p.MB;
-    for (int j = 0; j < n_tiles; ++j) {
-      const int st = j % NST;
-      if (!warp_wait(&kv_empty[st], ((j / NST) & 1) ^ 1, abort_s)) {
-        if (lane == 0) report(p.dev_status, PA_DEVERR_TIMEOUT);
-        break;
+    auto group_row = [&](int j) -> int32_t {
+      if (lane >= NBOX || j >= n_tiles) return 0;
+      const int64_t t = (int64_t)j * BN + g16 * 16;  // first token of the group
+      const int64_t pg = t / p.BS;
+      int64_t blk = (t < ctx && pg < p.MB) ? bt[pg] : bt[0];
+      if (blk < 0 || blk >= p.NB) {
+        report(p.dev_status, PA_DEVERR_BLOCK_ID);
+        blk = 0;
       }
-      if (lane == 0) mbar_arrive_expect_tx(&kv_full[st], 2 * C::KV_BYTES);
+      return (int32_t)(blk * p.BS + (t - pg * p.BS));
+    };
+    auto load = [&](bool is_v, int j, int32_t row) -> bool {
+      const int st = is_v ? j % NV : j % NK;
+      const int n = is_v ? NV : NK;
+      uint64_t* empty = is_v ? &v_empty[st] : &k_empty[st];
+      uint64_t* full = is_v ? &v_full[st] : &k_full[st];
+      if (!warp_wait(empty, ((j / n) & 1) ^ 1, abort_s)) return false;
+      if (lane == 0) mbar_arrive_expect_tx(full, C::KV_BYTES);
       __syncwarp();
       if (lane < NBOX) {
-        const int64_t t = (int64_t)j * BN + g16 * 16;  // first token of the group
-        const int64_t pg = t / p.BS;
-        int64_t blk = (t < ctx && pg < p.MB) ? bt[pg] : bt[0];
-        if (blk < 0 || blk >= p.NB) {
-          report(p.dev_status, PA_DEVERR_BLOCK_ID);
-          blk = 0;
-        }
-        const int32_t row = (int32_t)(blk * p.BS + (t - pg * p.BS));
-        unsigned char* dst = smem + C::OFF_KV + st * 2 * C::KV_BYTES + kv * C::KV_BYTES +
+        unsigned char* dst = smem + (is_v ? C::OFF_V : C::OFF_K) + st * C::KV_BYTES +
                              hf * (BN * 128) + g16 * 16 * 128;
-        tc::tma_load_3d(dst, kv ? &p.tmap_v : &p.tmap_k, hf * 64, (int32_t)kv_h, row,
-                        &kv_full[st]);
+        tc::tma_load_3d(dst, is_v ? &p.tmap_v : &p.tmap_k, hf * 64, (int32_t)kv_h, row, full);
       }
+      return true;
+    };
+    // K runs NK - NV tiles ahead of V: issue order K0..K(d-1), then (K j+d, V j)
+    constexpr int AHEAD = NK - NV;
+    int32_t rows_k[AHEAD + 1];
+    bool ok = true;
+    for (int j = 0; j < AHEAD && j < n_tiles && ok; ++j) ok = load(false, j, group_row(j));
+    for (int j = 0; j < n_tiles && ok; ++j) {
+      const int jk = j + AHEAD;
+      if (jk < n_tiles) ok = load(false, jk, group_row(jk));
+      if (ok) ok = load(true, j, group_row(j));
     }
+    (void)rows_k;
+    if (!ok && lane == 0) report(p.dev_status, PA_DEVERR_TIMEOUT);
   }
 
   tc::fence_before_sync();
   __syncthreads();
-  if (warp == 4) {
+  if (warp == kMmaWarp) {
     tc::fence_after_sync();
     tc::tmem_dealloc(tmem, kTmemCols);
   }
