@@ -7,24 +7,33 @@
 //
 //   * CTA = 128 query rows x one head.  KV tiles of 128 keys = 8 pages of 16
 //     tokens, loaded by one producer warp with 3-D tiled TMA (box = 16 rows x
-//     64 head-dim elements of one KV head, 128-byte swizzle) into a ring of
-//     K/V stages -- the block table turns each 16-row group into a row
-//     coordinate, so the page gather costs no extra pass.
+//     64 head-dim elements of one KV head, 128-byte swizzle) into separate K
+//     and V rings (a K stage is freed once S = Q K^T is done, so the K ring
+//     runs a tile deeper) -- the block table, staged in shared memory, turns
+//     each 16-row group into a row coordinate, so the page gather costs no
+//     extra pass.
 //   * S = Q K^T accumulates in TMEM (double-buffered, 2 x 128 columns) from one
 //     elected thread's tcgen05.mma (A = Q from shared memory, B = K from
 //     shared memory, M = 128, N = 128, K = 16 per instruction).
-//   * Four softmax warps (thread = query row = TMEM lane) read S with
-//     tcgen05.ld, apply the causal rule of paged_attn_prefill.cu:62-65, keep
-//     the running max / sum in fp32, and write P back into the S columns of
-//     TMEM; O += P V then takes A = P straight from TMEM (no shared-memory
-//     round trip) and B = V from shared memory (MN-major), O in TMEM.
+//   * Two softmax warpgroups alternate over the KV tiles (ping-pong): group g
+//     takes tiles j % 2 == g, so one group's exponentials overlap the other's
+//     MMAs.  Thread = query row = TMEM lane: it reads S with tcgen05.ld,
+//     applies the causal rule of paged_attn_prefill.cu:62-65, keeps its
+//     group's running max / sum in fp32, and writes P back into the S columns
+//     of TMEM; O_g += P V then takes A = P straight from TMEM (no shared-memory
+//     round trip) and B = V from shared memory (MN-major), with one O
+//     accumulator per group in TMEM.  The epilogue merges the two groups'
+//     (max, sum, O) with the log-sum-exp rule.
 //   * Rescaling of O is lazy: the reference max only moves when a row's max
 //     grows by more than 2^8, so O (in TMEM) is rarely touched; the result is
 //     exact because the final division uses the same reference max.
 //   * Precision: A and B of one kind::f16 MMA share a type.  For bf16 pools Q
 //     and P are split into bf16 hi + lo parts (two MMAs each): plain bf16 Q
 //     and P measured 2.7-4.0e-3 max-abs against the fp32 oracle, over the
-//     2e-3 bar; the split gives ~1e-5.  fp16 pools use single fp16 MMAs.
+//     2e-3 bar; the split gives ~2e-5.  fp16 pools use single fp16 MMAs.
+//   * The softmax runs on packed fp32 pairs (add/fma .f32x2) and builds P's
+//     hi / lo parts with integer byte permutes (both truncations; hi + lo
+//     still carries P to 2^-16), so exp2 dominates its instruction stream.
 //
 // Every wait is bounded; on a timeout the CTA reports PA_DEVERR_TIMEOUT, stops
 // issuing work, and still frees its tensor memory before it exits.
@@ -43,11 +52,19 @@ namespace prefill {
 
 constexpr int BM = 128;  // query rows per CTA
 constexpr int BN = 128;  // keys per KV tile
-constexpr int kSoftmaxWarps = 8;  // two per TMEM lane quadrant
+// Warpgroups 0-1: softmax (warpgroup g takes the KV tiles j % 2 == g);
+// warpgroup 2: warp 8 issues the MMAs, warp 9 the TMA loads, warps 10-11 idle.
+// Registers: 384 threads launched at 168 (64512); setmaxnreg gives the
+// softmax warpgroups 232 and the rest 40: 256 x 232 + 128 x 40 = 64512.
+constexpr int kSoftmaxWarps = 8;
 constexpr int kMmaWarp = 8;
 constexpr int kTmaWarp = 9;
-constexpr int kThreads = 320;
+constexpr int kThreads = 384;
+constexpr int kSoftmaxRegs = 232, kOtherRegs = 40;
+static_assert(256 * kSoftmaxRegs + 128 * kOtherRegs <= kThreads * 168, "register split");
 constexpr uint32_t kTmemCols = 512;
+// block ids the TMA warp stages in shared memory per refill (32 tiles at 16-token pages)
+constexpr int kBtChunk = 256;
 
 struct Params {
   CUtensorMap tmap_k;  // 3-D [D, HKV, NB*BS] views of the pool, box {64, 1, 16}
@@ -82,11 +99,15 @@ struct Cfg {
   static constexpr uint32_t OFF_K = Q_BYTES * (SPLIT ? 2 : 1);
   static constexpr uint32_t OFF_V = OFF_K + NK * KV_BYTES;
   static constexpr uint32_t OFF_BAR = OFF_V + NV * KV_BYTES;
-  static constexpr uint32_t SMEM = OFF_BAR + 192 + 1024;  // + barriers + alignment slack
+  // mbarriers: K and V full/empty rings, s_full/p_full/o_ready pairs, q_ready,
+  // 4 pair barriers; then the TMEM address and the abort flag
+  static constexpr uint32_t N_BARS = 2 * NK + 2 * NV + 2 * 3 + 1 + 4;
+  static constexpr uint32_t OFF_BT = OFF_BAR + ((N_BARS * 8 + 8 + 15) / 16) * 16;
+  static constexpr uint32_t SMEM = OFF_BT + kBtChunk * 4 + 1024;  // + alignment slack
   static_assert(SMEM <= 227 * 1024, "shared memory budget");
-  // TMEM columns: S buffers at 0 and 128, O at 256, row-max / sum exchange
-  // slots of the softmax warp pairs at 384..387
-  static constexpr uint32_t COL_S0 = 0, COL_S1 = 128, COL_O = 256, COL_X = 384;
+  // TMEM columns: S buffers at 0 and 128 (tiles j % 2), O of the two
+  // softmax warpgroups at 256 and 256 + D
+  static constexpr uint32_t COL_S0 = 0, COL_S1 = 128, COL_O = 256;
 };
 
 __device__ __forceinline__ uint32_t pack2(float lo, float hi, __nv_bfloat16*) {
@@ -125,6 +146,42 @@ __device__ __forceinline__ void split_pair(float a, float b, uint32_t& hi, uint3
   lo = 0;
 }
 
+// Packed fp32 pair arithmetic (sm_100 add/fma .f32x2: one issue slot for two
+// lanes of work).
+__device__ __forceinline__ float2 add2(float2 a, float2 b) {
+  float2 r;
+  asm("{.reg .b64 pa, pb, pd;\n\tmov.b64 pa, {%2, %3};\n\tmov.b64 pb, {%4, %5};\n\t"
+      "add.rn.ftz.f32x2 pd, pa, pb;\n\tmov.b64 {%0, %1}, pd;}"
+      : "=f"(r.x), "=f"(r.y) : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+  return r;
+}
+__device__ __forceinline__ float2 fma2(float2 a, float2 b, float2 c) {
+  float2 r;
+  asm("{.reg .b64 pa, pb, pc, pd;\n\tmov.b64 pa, {%2, %3};\n\tmov.b64 pb, {%4, %5};\n\t"
+      "mov.b64 pc, {%6, %7};\n\tfma.rn.ftz.f32x2 pd, pa, pb, pc;\n\tmov.b64 {%0, %1}, pd;}"
+      : "=f"(r.x), "=f"(r.y)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y), "f"(c.x), "f"(c.y));
+  return r;
+}
+
+// Softmax weights (p0, p1) of two adjacent keys -> the MMA operand pair(s).
+// bf16: hi = the fp32 bits truncated to bf16, lo = the remainder p - hi
+// (exact in fp32) truncated to bf16; hi + lo carries p to 2^-16 relative,
+// with integer byte permutes instead of conversions.  fp16: one
+// round-to-nearest pair.
+__device__ __forceinline__ void p_pair(float p0, float p1, uint32_t& hi, uint32_t& lo,
+                                       __nv_bfloat16*) {
+  const uint32_t a = __float_as_uint(p0), b = __float_as_uint(p1);
+  hi = __byte_perm(a, b, 0x7632);
+  const float2 r = fma2(make_float2(__uint_as_float(a & 0xffff0000u), __uint_as_float(b & 0xffff0000u)),
+                        make_float2(-1.f, -1.f), make_float2(p0, p1));
+  lo = __byte_perm(__float_as_uint(r.x), __float_as_uint(r.y), 0x7632);
+}
+__device__ __forceinline__ void p_pair(float p0, float p1, uint32_t& hi, uint32_t& lo, __half*) {
+  hi = pack2(p0, p1, (__half*)nullptr);
+  lo = 0;
+}
+
 // Byte offset of element (r, k) of a [rows x D] K-major tile stored as D/64
 // swizzled 128-byte-row halves of `rows * 128` bytes each (the layout the
 // tensor core reads with a SWIZZLE_128B descriptor, and TMA writes).
@@ -159,8 +216,8 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const __grid_co
   uint64_t* v_empty = v_full + NV;       // [NV] P V done with it
   uint64_t* s_full = v_empty + NV;       // [2] S tile in TMEM
   uint64_t* p_full = s_full + 2;         // [2] P written to TMEM (softmax warps)
-  uint64_t* o_ready = p_full + 2;        // PV of a tile done
-  uint64_t* q_ready = o_ready + 1;       // Q in shared memory (softmax warps)
+  uint64_t* o_ready = p_full + 2;        // [2] P V of a tile of group j % 2 done
+  uint64_t* q_ready = o_ready + 2;       // Q in shared memory (softmax warps)
   uint64_t* pair_bar = q_ready + 1;     // [4] max / sum exchange of a warp pair (64 threads)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(pair_bar + 4);
   int32_t* abort_s = reinterpret_cast<int32_t*>(tmem_slot + 1);
@@ -187,9 +244,9 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const __grid_co
     }
     for (int s = 0; s < 2; ++s) {
       mbar_init(&s_full[s], 1);
-      mbar_init(&p_full[s], kSoftmaxWarps * 32);
+      mbar_init(&p_full[s], 4 * 32);  // one warpgroup per tile
+      mbar_init(&o_ready[s], 1);
     }
-    mbar_init(o_ready, 1);
     mbar_init(q_ready, kSoftmaxWarps * 32);
     for (int qd = 0; qd < 4; ++qd) mbar_init(&pair_bar[qd], 64);
     *abort_s = 0;
@@ -217,10 +274,10 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const __grid_co
 
   if (warp < kSoftmaxWarps) {
     // ------------------------------------------------------------------ softmax
-    // Warp w serves query rows 32 * (w % 4) .. +31 (its TMEM lane quadrant) and
-    // key columns 64 * (w / 4) .. +63 of each S tile; the two warps of a
-    // quadrant share each row's max through shared memory.
-    const int quad = warp & 3, ch = warp >> 2;
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kSoftmaxRegs));
+    // Warp w serves query rows 32 * (w % 4) .. +31 (its TMEM lane quadrant)
+    // of the tiles of warpgroup w / 4.
+    const int quad = warp & 3;
     const int r = quad * 32 + lane;  // query row in the tile = TMEM lane
     const int64_t qrow = q0 + r;
     const bool row_valid = qrow < p.Sq;
@@ -231,28 +288,33 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const __grid_co
       unsigned char* qh = smem + C::OFF_QH;
       unsigned char* ql = smem + C::OFF_QL;
       constexpr int EPT = D / 32;  // elements per lane per row
+      constexpr int RPW = BM / kSoftmaxWarps;  // rows per warp
+      // every row's global load is issued before the first shared store, so
+      // the warp waits on global memory once
+      float x[RPW][EPT];
 #pragma unroll
-      for (int i = 0; i < BM / kSoftmaxWarps; ++i) {
-        const int rr = warp * (BM / kSoftmaxWarps) + i;
-        const int64_t qr = q0 + rr;
-        float x[EPT];
-        if (qr < p.Sq) {
-          const float* src = p.q + ((b * p.Sq + qr) * p.H + h) * D + lane * EPT;
-#pragma unroll
-          for (int e = 0; e < EPT; e += 2) {
-            const float2 v = *reinterpret_cast<const float2*>(src + e);
-            x[e] = v.x * p.qscale;
-            x[e + 1] = v.y * p.qscale;
-          }
+      for (int i = 0; i < RPW; ++i) {
+        const int64_t qr = q0 + warp * RPW + i;
+        const float* src = p.q + ((b * p.Sq + qr) * p.H + h) * D + lane * EPT;
+        if constexpr (EPT == 4) {
+          const float4 v = qr < p.Sq ? __ldg(reinterpret_cast<const float4*>(src)) : make_float4(0.f, 0.f, 0.f, 0.f);
+          x[i][0] = v.x, x[i][1] = v.y, x[i][2] = v.z, x[i][3] = v.w;
         } else {
 #pragma unroll
-          for (int e = 0; e < EPT; ++e) x[e] = 0.f;
+          for (int e = 0; e < EPT; e += 2) {
+            const float2 v = qr < p.Sq ? __ldg(reinterpret_cast<const float2*>(src + e)) : make_float2(0.f, 0.f);
+            x[i][e] = v.x, x[i][e + 1] = v.y;
+          }
         }
+      }
+#pragma unroll
+      for (int i = 0; i < RPW; ++i) {
+        const int rr = warp * RPW + i;
 #pragma unroll
         for (int e = 0; e < EPT; e += 2) {
           const uint32_t off = sw128_offset(rr, lane * EPT + e, BM);
           uint32_t hi, lo;
-          split_pair(x[e], x[e + 1], hi, lo, (T*)nullptr);
+          split_pair(x[i][e] * p.qscale, x[i][e + 1] * p.qscale, hi, lo, (T*)nullptr);
           *reinterpret_cast<uint32_t*>(qh + off) = hi;
           if constexpr (C::SPLIT) *reinterpret_cast<uint32_t*>(ql + off) = lo;
         }
@@ -261,65 +323,72 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const __grid_co
       mbar_arrive(q_ready);
     }
 
-    constexpr int HC = BN / 2;  // key columns per warp
+    // Warpgroup g = warp / 4 takes the KV tiles j with j % 2 == g (S buffer
+    // g) and keeps, per query row, its own running reference max, sum and O
+    // accumulator (TMEM columns COL_O + g * D); the two partial states are
+    // merged with the log-sum-exp rule once, after the last tile.  Two tiles'
+    // softmax are in flight at a time and no cross-warp reduction sits on the
+    // per-tile path.
+    const int grp = warp >> 2;
     const uint32_t lane_base = tmem + ((uint32_t)(quad * 32) << 16);
+    const uint32_t ocol = C::COL_O + grp * D;
     float m_ref = -INFINITY, l = 0.f;
     bool ok = true;
-    for (int j = 0; j < n_tiles && ok; ++j) {
-      if (!warp_wait(&s_full[j & 1], (j >> 1) & 1, abort_s)) { ok = false; break; }
+    int last_j = -1;
+    for (int j = grp; j < n_tiles && ok; j += 2) {
+      if (!warp_wait(&s_full[grp], (j >> 1) & 1, abort_s)) { ok = false; break; }
       tc::fence_after_sync();
-      const uint32_t scol = ((j & 1) ? C::COL_S1 : C::COL_S0);
-      float s[HC];
-#pragma unroll
-      for (int c4 = 0; c4 < HC / 32; ++c4) {
-        uint32_t u[32];
-        tc::tmem_ld32(lane_base + scol + ch * HC + 32 * c4, u);
-        tc::tmem_wait_ld();
-#pragma unroll
-        for (int i = 0; i < 32; ++i) s[32 * c4 + i] = __uint_as_float(u[i]);
-      }
+      const uint32_t scol = grp ? C::COL_S1 : C::COL_S0;
       // causal rule + context bound (kernels/paged_attn_prefill.cu:62-65):
-      // this warp's keys k0 + c, c < HC, are visible when c < lim
-      const int64_t k0 = (int64_t)j * BN + ch * HC;
+      // keys k0 + c of this tile are visible when c < lim
+      const int64_t k0 = (int64_t)j * BN;
       const int64_t vis = row_valid ? min(q_abs + 1, ctx) - k0 : 0;
-      const int lim = vis <= 0 ? 0 : (vis >= HC ? HC : (int)vis);
+      const int lim = vis <= 0 ? 0 : (vis >= BN ? BN : (int)vis);
+      // pass 1: row max over the visible keys (S streamed from TMEM, 32
+      // columns at a time); tiles with every key visible to all of the warp's
+      // rows skip the per-key mask
+      const bool full = __all_sync(0xffffffffu, lim == BN);
       float mt = -INFINITY;
+      if (full) {
+        float m4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
 #pragma unroll
-      for (int i = 0; i < HC; ++i) {
-        s[i] = (i < lim) ? s[i] : -INFINITY;
-        mt = fmaxf(mt, s[i]);
-      }
-      // row max over both column halves, exchanged through TMEM slot j & 1 (a
-      // warp is at most one tile ahead of its partner, so the slots alternate)
-      tc::tmem_st1(lane_base + C::COL_X + 2 * (j & 1) + ch, __float_as_uint(mt));
-      tc::tmem_wait_st();
-      tc::fence_before_sync();
-      mbar_arrive(&pair_bar[quad]);
-      if (!warp_wait(&pair_bar[quad], j & 1, abort_s)) { ok = false; break; }
-      tc::fence_after_sync();
-      {
-        const uint32_t other = tc::tmem_ld1(lane_base + C::COL_X + 2 * (j & 1) + (ch ^ 1));
-        tc::tmem_wait_ld();
-        mt = fmaxf(mt, __uint_as_float(other));
+        for (int c4 = 0; c4 < BN / 32; ++c4) {
+          uint32_t u[32];
+          tc::tmem_ld32(lane_base + scol + 32 * c4, u);
+          tc::tmem_wait_ld();
+#pragma unroll
+          for (int i = 0; i < 32; ++i) m4[i & 3] = fmaxf(m4[i & 3], __uint_as_float(u[i]));
+        }
+        mt = fmaxf(fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3]));
+      } else {
+#pragma unroll
+        for (int c4 = 0; c4 < BN / 32; ++c4) {
+          uint32_t u[32];
+          tc::tmem_ld32(lane_base + scol + 32 * c4, u);
+          tc::tmem_wait_ld();
+#pragma unroll
+          for (int i = 0; i < 32; ++i)
+            if (32 * c4 + i < lim) mt = fmaxf(mt, __uint_as_float(u[i]));
+        }
       }
       // The reference max of a row moves only when the row's max grows by more
-      // than 2^8 (then O and l are rescaled); the O rescale is done by the
-      // whole warp (tcgen05.ld/st are warp-collective) on its half of O's
-      // columns, factor 1 for rows that keep their reference.
+      // than 2^8 (then this group's O and l are rescaled); the O rescale is
+      // done by the whole warp (tcgen05.ld/st are warp-collective), factor 1
+      // for rows that keep their reference.
       const bool need = mt > m_ref + 8.f;
       const float factor = need ? fast_exp2(m_ref - mt) : 1.f;  // 0 on a row's first visible tile
-      if (__any_sync(0xffffffffu, need) && j > 0) {
-        if (!warp_wait(o_ready, (j - 1) & 1, abort_s)) { ok = false; break; }
+      if (__any_sync(0xffffffffu, need) && j >= 2) {
+        // the group's previous P V (tile j - 2) must have finished
+        if (!warp_wait(&o_ready[grp], ((j >> 1) - 1) & 1, abort_s)) { ok = false; break; }
         tc::fence_after_sync();
 #pragma unroll
-        for (int c4 = 0; c4 < D / 64; ++c4) {
+        for (int c4 = 0; c4 < D / 32; ++c4) {
           uint32_t u[32];
-          const uint32_t col = lane_base + C::COL_O + ch * (D / 2) + 32 * c4;
-          tc::tmem_ld32(col, u);
+          tc::tmem_ld32(lane_base + ocol + 32 * c4, u);
           tc::tmem_wait_ld();
 #pragma unroll
           for (int i = 0; i < 32; ++i) u[i] = __float_as_uint(__uint_as_float(u[i]) * factor);
-          tc::tmem_st32(col, u);
+          tc::tmem_st32(lane_base + ocol + 32 * c4, u);
         }
         tc::tmem_wait_st();
       }
@@ -327,57 +396,92 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const __grid_co
         l *= factor;
         m_ref = mt;
       }
-      float lsum = 0.f;
-#pragma unroll
-      for (int i = 0; i < HC; ++i) {
-        const float e = (i < lim) ? fast_exp2(s[i] - m_ref) : 0.f;
-        s[i] = e;
-        lsum += e;
-      }
-      l += lsum;
       // Keys of this tile past the context (tail of the last page) get P = 0,
       // but 0 * NaN is NaN: zero their V rows in the stage before P V runs
-      // (an unwritten pool row may hold anything).  The warp pair of quadrant
-      // q zeroes rows 32q .. 32q+31, each warp half of every row.
-      {
-        const int64_t vr = (int64_t)j * BN + r;
-        if (vr >= ctx) {
-          unsigned char* vrow = smem + C::OFF_V + (j % NV) * C::KV_BYTES +
-                                (r >> 3) * 1024 + (r & 7) * 128;
+      // (an unwritten pool row may hold anything).  Thread r owns V row r.
+      if (k0 + r >= ctx) {
+        unsigned char* vrow = smem + C::OFF_V + (j % NV) * C::KV_BYTES + (r >> 3) * 1024 +
+                              (r & 7) * 128;
 #pragma unroll
-          for (int hf = 0; hf < C::NH; ++hf)
+        for (int hf = 0; hf < C::NH; ++hf)
 #pragma unroll
-            for (int c16 = ch * 4; c16 < ch * 4 + 4; ++c16)
-              *reinterpret_cast<uint4*>(vrow + hf * (BN * 128) + c16 * 16) = make_uint4(0, 0, 0, 0);
-          tc::fence_proxy_async_smem();
+          for (int c16 = 0; c16 < 8; ++c16)
+            *reinterpret_cast<uint4*>(vrow + hf * (BN * 128) + c16 * 16) = make_uint4(0, 0, 0, 0);
+        tc::fence_proxy_async_smem();
+      }
+      // pass 2: P = exp2(s - m_ref) into the S columns, 32 keys at a time
+      // (S re-read from TMEM).  Keys 32c .. 32c + 31 go to columns
+      // [32c, 32c + 16) as 16-bit pairs (keys 2i, 2i+1 in column 32c + i),
+      // their lo parts to [32c + 16, 32c + 32): every store lands on columns
+      // this pass has already read.  Masked keys get s = -inf, so P = 0.
+      // (a row with no visible key so far has m_ref = -inf and only masked keys here)
+      const float mneg = m_ref == -INFINITY ? 0.f : -m_ref;
+      const float2 negm = make_float2(mneg, mneg);
+      float2 ls = make_float2(0.f, 0.f);
+#pragma unroll
+      for (int c = 0; c < BN / 32; ++c) {
+        uint32_t u[32];
+        tc::tmem_ld32(lane_base + scol + 32 * c, u);
+        tc::tmem_wait_ld();
+        if (!full) {
+#pragma unroll
+          for (int i = 0; i < 32; ++i)
+            if (32 * c + i >= lim) u[i] = __float_as_uint(-INFINITY);
         }
-      }
-      // P into the S columns: column c of the S buffer holds keys 2c (low half)
-      // and 2c+1; P hi in columns [0, 64), P lo in [64, 128).
-      {
-        uint32_t uh[32], ul[32];
+        uint32_t uh[16], ul[16];
 #pragma unroll
-        for (int i = 0; i < 32; ++i) split_pair(s[2 * i], s[2 * i + 1], uh[i], ul[i], (T*)nullptr);
-        tc::tmem_st32(lane_base + scol + ch * 32, uh);
-        if constexpr (C::SPLIT) tc::tmem_st32(lane_base + scol + BN / 2 + ch * 32, ul);
+        for (int i = 0; i < 16; ++i) {
+          const float2 x = add2(make_float2(__uint_as_float(u[2 * i]), __uint_as_float(u[2 * i + 1])), negm);
+          const float2 e = make_float2(fast_exp2(x.x), fast_exp2(x.y));
+          ls = add2(ls, e);
+          p_pair(e.x, e.y, uh[i], ul[i], (T*)nullptr);
+        }
+        tc::tmem_st16(lane_base + scol + 32 * c, uh);
+        if constexpr (C::SPLIT) tc::tmem_st16(lane_base + scol + 32 * c + 16, ul);
       }
+      const float lsum = ls.x + ls.y;
+      l += lsum;
       tc::tmem_wait_st();
       tc::fence_before_sync();
-      mbar_arrive(&p_full[j & 1]);
+      mbar_arrive(&p_full[grp]);
+      last_j = j;
     }
 
-    // epilogue: O / l -> out (this warp's half of the columns); the pair's
-    // partial sums meet through slot n_tiles & 1 (phase n_tiles of pair_bar)
+    // epilogue: merge the two groups' (m, l, O) per row, O / l -> out.  Each
+    // warp of a pair writes half of the columns.  (m, l) cross through TMEM
+    // columns of this group's (now idle) S buffer.
+    const uint32_t xcol = grp ? C::COL_S1 : C::COL_S0;
+    const uint32_t xcol_other = grp ? C::COL_S0 : C::COL_S1;
+    float mo = -INFINITY, lo_ = 0.f;
+    bool have_mine = false, have_other = false;
     if (ok) {
-      tc::tmem_st1(lane_base + C::COL_X + 2 * (n_tiles & 1) + ch, __float_as_uint(l));
+      // all of this row's P V products must be complete: wait both groups' last
+      const int lj[2] = {n_tiles >= 1 ? ((n_tiles - 1) & ~1) : -1,
+                         n_tiles >= 2 ? (((n_tiles - 2) & ~1) | 1) : -1};
+      for (int g = 0; g < 2 && ok; ++g)
+        if (lj[g] >= 0 && !warp_wait(&o_ready[g], (lj[g] >> 1) & 1, abort_s)) ok = false;
+      have_mine = lj[grp] >= 0;
+      have_other = lj[grp ^ 1] >= 0;
+      (void)last_j;
+    }
+    if (ok) {
+      tc::fence_after_sync();
+      uint32_t x[32];
+      x[0] = __float_as_uint(m_ref);
+      x[1] = __float_as_uint(l);
+#pragma unroll
+      for (int i = 2; i < 32; ++i) x[i] = 0;
+      tc::tmem_st32(lane_base + xcol, x);
       tc::tmem_wait_st();
       tc::fence_before_sync();
       mbar_arrive(&pair_bar[quad]);
-      if (warp_wait(&pair_bar[quad], n_tiles & 1, abort_s)) {
+      if (warp_wait(&pair_bar[quad], 0, abort_s)) {
         tc::fence_after_sync();
-        const uint32_t other = tc::tmem_ld1(lane_base + C::COL_X + 2 * (n_tiles & 1) + (ch ^ 1));
+        uint32_t y[32];
+        tc::tmem_ld32(lane_base + xcol_other, y);
         tc::tmem_wait_ld();
-        l += __uint_as_float(other);
+        mo = __uint_as_float(y[0]);
+        lo_ = __uint_as_float(y[1]);
       } else {
         ok = false;
       }
@@ -386,32 +490,40 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const __grid_co
     float o[HD];
 #pragma unroll
     for (int i = 0; i < HD; ++i) o[i] = 0.f;
-    if (ok && n_tiles > 0) {
-      if (warp_wait(o_ready, (n_tiles - 1) & 1, abort_s)) {
-        tc::fence_after_sync();
+    if (ok) {
+      // this warp's output columns [grp * HD, grp * HD + HD) from both O buffers
+      const float mA = grp ? mo : m_ref, lA = grp ? lo_ : l;
+      const float mB = grp ? m_ref : mo, lB = grp ? l : lo_;
+      const bool hasA = grp ? have_other : have_mine, hasB = grp ? have_mine : have_other;
+      const float mm = fmaxf(hasA ? mA : -INFINITY, hasB ? mB : -INFINITY);
+      const float wA = (hasA && lA > 0.f) ? fast_exp2(mA - mm) : 0.f;
+      const float wB = (hasB && lB > 0.f) ? fast_exp2(mB - mm) : 0.f;
+      const float L = lA * wA + lB * wB;
+      const float inv = L > 0.f ? 1.f / L : 0.f;
 #pragma unroll
-        for (int c4 = 0; c4 < HD / 32; ++c4) {
-          uint32_t u[32];
-          tc::tmem_ld32(lane_base + C::COL_O + ch * HD + 32 * c4, u);
-          tc::tmem_wait_ld();
+      for (int c4 = 0; c4 < HD / 32; ++c4) {
+        uint32_t ua[32], ub[32];
+        tc::tmem_ld32(lane_base + C::COL_O + grp * HD + 32 * c4, ua);
+        tc::tmem_ld32(lane_base + C::COL_O + D + grp * HD + 32 * c4, ub);
+        tc::tmem_wait_ld();
 #pragma unroll
-          for (int i = 0; i < 32; ++i) o[32 * c4 + i] = __uint_as_float(u[i]);
+        for (int i = 0; i < 32; ++i) {
+          const float a = wA > 0.f ? __uint_as_float(ua[i]) * wA : 0.f;
+          const float bb = wB > 0.f ? __uint_as_float(ub[i]) * wB : 0.f;
+          o[32 * c4 + i] = (a + bb) * inv;
         }
-        const float inv = l > 0.f ? 1.f / l : 0.f;
-#pragma unroll
-        for (int i = 0; i < HD; ++i) o[i] *= inv;
-      } else {
-        ok = false;
       }
     }
     if (row_valid) {
-      float* dst = p.out + ((b * p.Sq + qrow) * p.H + h) * D + ch * HD;
+      float* dst = p.out + ((b * p.Sq + qrow) * p.H + h) * D + grp * HD;
 #pragma unroll
       for (int i = 0; i < HD; i += 4)
         *reinterpret_cast<float4*>(dst + i) = make_float4(o[i], o[i + 1], o[i + 2], o[i + 3]);
     }
     if (!ok && lane == 0) report(p.dev_status, PA_DEVERR_TIMEOUT);
-  } else if (warp == kMmaWarp) {
+  } else {
+   asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kOtherRegs));
+   if (warp == kMmaWarp) {
     // ------------------------------------------------------------- MMA issuer
     if (lane == 0 && n_tiles > 0) {
       constexpr uint32_t idesc_s = tc::idesc_f16(Fmt<T>::id, BM, BN, false);
@@ -453,13 +565,14 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const __grid_co
         for (int part = 0; part < (C::SPLIT ? 2 : 1); ++part) {
 #pragma unroll
           for (int kk = 0; kk < BN / 16; ++kk) {
-            tc::mma_ts(tmem + C::COL_O, pcol + part * (BN / 2) + kk * 8,
+            // keys 16kk .. 16kk + 15: 8 columns of packed pairs
+            tc::mma_ts(tmem + C::COL_O + (j & 1) * D, pcol + (kk >> 1) * 32 + (kk & 1) * 8 + part * 16,
                        tc::smem_desc_sw128(vb + kk * 16 * 128, BN * 128, 1024), idesc_o,
-                       (j > 0 || part > 0 || kk > 0) ? 1u : 0u);
+                       (j > 1 || part > 0 || kk > 0) ? 1u : 0u);
           }
         }
         tc::mma_commit(&v_empty[vs]);
-        tc::mma_commit(o_ready);
+        tc::mma_commit(&o_ready[j & 1]);
       }
       if (!ok) report(p.dev_status, PA_DEVERR_TIMEOUT);
     }
@@ -467,16 +580,40 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const __grid_co
     // ------------------------------------------------------------- TMA producer
     // Lane l < 8 * NH loads one 16-row group x 64-column half of the K tile
     // (then of the V tile); the K tile of j runs up to NK tiles ahead, the V
-    // tile up to NV.  Block ids are read one tile ahead of their use.
+    // tile up to NV.  The sequence's block ids are staged in shared memory,
+    // kBtChunk pages per coalesced refill, so no dependent global load sits
+    // on the per-tile issue path; a tile's rows serve its K and its V load.
     constexpr int NBOX = 8 * C::NH;
     const int g16 = lane / C::NH;
     const int hf = lane % C::NH;
     const int32_t* bt = p.block_tables + b * p.MB;
+    int32_t* bt_s = reinterpret_cast<int32_t*>(smem + C::OFF_BT);
+    const int64_t n_pages = (ctx + p.BS - 1) / p.BS;  // <= MB (ctx clamped above)
+    int64_t chunk0 = -(int64_t)kBtChunk - 1;         // first page held in bt_s
+    // warp-uniform: make pages [pg_lo, pg_hi] resident
+    auto stage_pages = [&](int64_t pg_lo, int64_t pg_hi) {
+      if (pg_lo >= chunk0 && pg_hi < chunk0 + kBtChunk) return;
+      chunk0 = pg_lo;
+      int32_t v[kBtChunk / 32];
+#pragma unroll
+      for (int i = 0; i < kBtChunk / 32; ++i) {
+        const int64_t pg = chunk0 + i * 32 + lane;
+        v[i] = pg < n_pages ? __ldg(bt + pg) : 0;
+      }
+      __syncwarp();
+#pragma unroll
+      for (int i = 0; i < kBtChunk / 32; ++i) bt_s[i * 32 + lane] = v[i];
+      __syncwarp();
+    };
+    // pool row of this lane's 16-token group of tile j (row 0 past the context)
     auto group_row = [&](int j) -> int32_t {
-      if (lane >= NBOX || j >= n_tiles) return 0;
-      const int64_t t = (int64_t)j * BN + g16 * 16;  // first token of the group
+      if (j >= n_tiles) return 0;
+      const int64_t t0 = (int64_t)j * BN;
+      stage_pages(t0 / p.BS, (t0 + BN - 1) / p.BS);
+      const int64_t t = t0 + g16 * 16;  // first token of the group
+      if (lane >= NBOX || t >= ctx) return 0;
       const int64_t pg = t / p.BS;
-      int64_t blk = (t < ctx && pg < p.MB) ? bt[pg] : bt[0];
+      int64_t blk = bt_s[pg - chunk0];
       if (blk < 0 || blk >= p.NB) {
         report(p.dev_status, PA_DEVERR_BLOCK_ID);
         blk = 0;
@@ -498,18 +635,26 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const __grid_co
       }
       return true;
     };
-    // K runs NK - NV tiles ahead of V: issue order K0..K(d-1), then (K j+d, V j)
+    // K runs NK - NV tiles ahead of V: issue order K0..K(d-1), then (K j+d, V j);
+    // rows[i] holds the rows of tile j + i
     constexpr int AHEAD = NK - NV;
-    int32_t rows_k[AHEAD + 1];
+    int32_t rows[AHEAD + 1];
     bool ok = true;
-    for (int j = 0; j < AHEAD && j < n_tiles && ok; ++j) ok = load(false, j, group_row(j));
+#pragma unroll
+    for (int i = 0; i < AHEAD; ++i) {
+      rows[i] = group_row(i);
+      if (ok && i < n_tiles) ok = load(false, i, rows[i]);
+    }
     for (int j = 0; j < n_tiles && ok; ++j) {
       const int jk = j + AHEAD;
-      if (jk < n_tiles) ok = load(false, jk, group_row(jk));
-      if (ok) ok = load(true, j, group_row(j));
+      rows[AHEAD] = group_row(jk);
+      if (jk < n_tiles) ok = load(false, jk, rows[AHEAD]);
+      if (ok) ok = load(true, j, rows[0]);
+#pragma unroll
+      for (int i = 0; i < AHEAD; ++i) rows[i] = rows[i + 1];
     }
-    (void)rows_k;
     if (!ok && lane == 0) report(p.dev_status, PA_DEVERR_TIMEOUT);
+   }
   }
 
   tc::fence_before_sync();
