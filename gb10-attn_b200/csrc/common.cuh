@@ -193,6 +193,24 @@ __device__ __forceinline__ float fast_exp2(float x) {
   return y;
 }
 
+// Packed fp32 pair arithmetic (sm_100 add / fma .f32x2, round to nearest, no
+// flush): one issue slot does the work of two scalar instructions.
+__device__ __forceinline__ float2 add2(float2 a, float2 b) {
+  float2 r;
+  asm("{.reg .b64 pa, pb, pd;\n\tmov.b64 pa, {%2, %3};\n\tmov.b64 pb, {%4, %5};\n\t"
+      "add.rn.f32x2 pd, pa, pb;\n\tmov.b64 {%0, %1}, pd;}"
+      : "=f"(r.x), "=f"(r.y) : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+  return r;
+}
+__device__ __forceinline__ float2 fma2(float2 a, float2 b, float2 c) {
+  float2 r;
+  asm("{.reg .b64 pa, pb, pc, pd;\n\tmov.b64 pa, {%2, %3};\n\tmov.b64 pb, {%4, %5};\n\t"
+      "mov.b64 pc, {%6, %7};\n\tfma.rn.f32x2 pd, pa, pb, pc;\n\tmov.b64 {%0, %1}, pd;}"
+      : "=f"(r.x), "=f"(r.y)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y), "f"(c.x), "f"(c.y));
+  return r;
+}
+
 __device__ __forceinline__ void report(int32_t* dev_status, int bits) {
   if (dev_status) atomicOr(dev_status, bits);
 }

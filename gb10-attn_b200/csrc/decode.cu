@@ -55,6 +55,7 @@ constexpr uint32_t kRingBudget = 200 * 1024;  // bytes of stages per CTA
 
 struct Config {
   int QC, G, NS, NGC, nstage, threads, N;
+  int64_t n_grp;  // run counters for two-level merges (0: single-level merges)
   uint32_t row_bytes;
   size_t smem;
   const void* kernel;
@@ -63,12 +64,13 @@ struct Config {
 };
 
 static size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
+constexpr int64_t kMaxRunCounters = 16384;
 
 struct PlanParams {
   const int32_t* context_lens;
   int32_t* tile_off;   // [B + 1]
   int32_t* cta_seq;    // [N]
-  int32_t* counters;   // [NGC * B * NS]
+  int32_t* counters;   // [NGC * B * NS + N * 2 * NS]
   int32_t* abort_flag;
   float* out;          // rows of empty sequences are filled with empty_fill
   float* lse;
@@ -303,7 +305,11 @@ static int configure(const DecodeArgs& a, Config* c) {
   c->off_cta = off;
   off = align256(off + sizeof(int32_t) * (size_t)N);
   c->off_cnt = off;
-  off = align256(off + sizeof(int32_t) * (size_t)(c->NGC * rows * c->NS));
+  // per-(g-chunk, row, slot) merge counters, then per-(CTA, slot) run counters
+  // for two-level merges -- only while the plan kernel zeroes them in a few
+  // passes (automatic splitting: N = SMs x resident CTAs)
+  c->n_grp = (N * 2 * c->NS <= kMaxRunCounters) ? N * 2 * c->NS : 0;
+  off = align256(off + sizeof(int32_t) * ((size_t)c->NGC * rows * c->NS + (size_t)c->n_grp));
   c->off_part = off;
   off = align256(off + sizeof(float) * (size_t)N * 2 * c->NS * QC * (a.D + 2));
   c->total = off;
@@ -339,7 +345,7 @@ int launch(const DecodeArgs& a, void* ws, size_t ws_bytes, cudaStream_t stream) 
   pp.H = a.H;
   pp.D = a.D;
   pp.max_ctx = a.MB * a.BS;
-  pp.n_counters = (int64_t)c.NGC * pp.B * c.NS;
+  pp.n_counters = (int64_t)c.NGC * pp.B * c.NS + c.n_grp;
   pp.qlen = a.qlen;
   pp.NGC = c.NGC;
   pp.N = c.N;
@@ -368,6 +374,7 @@ int launch(const DecodeArgs& a, void* ws, size_t ws_bytes, cudaStream_t stream) 
   p.tile_off = pp.tile_off;
   p.cta_seq = pp.cta_seq;
   p.counters = pp.counters;
+  p.grp_counters = c.n_grp ? pp.counters + (int64_t)c.NGC * pp.B * c.NS : nullptr;
   p.abort_flag = pp.abort_flag;
   p.partials = reinterpret_cast<float*>(w + c.off_part);
   p.B = a.B * a.qlen;

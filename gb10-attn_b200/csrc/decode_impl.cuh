@@ -37,6 +37,7 @@ namespace pa {
 namespace decode {
 
 constexpr int kTT = 16;            // tokens per pipeline stage
+constexpr int kGroup = 8;          // pieces merged per step of a split sequence
 constexpr float kNegBig = -3.0e38f;  // the reference's "minus infinity" (paged_attn_v3.cu:20)
 
 struct Params {
@@ -51,6 +52,7 @@ struct Params {
   const int32_t* tile_off;       // [B + 1] tiles before sequence b (per g-chunk)
   const int32_t* cta_seq;        // [N] sequence holding each CTA's first tile
   int32_t* counters;             // [NGC * B * NS] merge arrival counters
+  int32_t* grp_counters;         // [N * 2 * NS] arrivals per run of kGroup pieces, or null
   int32_t* abort_flag;           // set when any pipeline wait times out
   float* partials;               // [N * 2 * NS * QC * (D + 2)]
   int64_t B, H, HKV, NB, MB, BS;
@@ -122,6 +124,60 @@ __host__ __device__ __forceinline__ int64_t cta_lo(int64_t c, int64_t T_all, int
 // CTA whose range holds global tile t < T_all: the largest c with cta_lo(c) <= t.
 __host__ __device__ __forceinline__ int64_t cta_of(int64_t t, int64_t T_all, int64_t N) {
   return T_all >= N ? ((t + 1) * N - 1) / T_all : t;
+}
+
+// Log-sum-exp merge of the partial states at ptr(c0), ptr(c0 + stride), ...
+// (count of them; layout [QC][D] un-normalised O, then QC maxima, then QC
+// sums).  One warp: lane k takes the (m, l) of states k, k + 32, ... so the
+// maxima and weights cost one round trip per 32 states; the O rows are then
+// read a few states at a time with the weights broadcast.  Every lane ends
+// with the merged maxima mg, sums lg and elements lane + 32k of O in o[k].
+template <int QC, int D, typename PtrFn>
+__device__ __forceinline__ void merge_pieces(PtrFn ptr, int64_t c0, int64_t stride, int64_t count,
+                                             int lane, float (&o)[QC * D / 32], float (&mg)[QC],
+                                             float (&lg)[QC]) {
+  constexpr int PER = QC * D / 32;
+#pragma unroll
+  for (int j = 0; j < QC; ++j) { mg[j] = kNegBig; lg[j] = 0.f; }
+  for (int64_t k = lane; k < count; k += 32) {
+    const float* pc = ptr(c0 + k * stride);
+#pragma unroll
+    for (int j = 0; j < QC; ++j) mg[j] = fmaxf(mg[j], __ldcg(pc + QC * D + j));
+  }
+#pragma unroll
+  for (int j = 0; j < QC; ++j)
+#pragma unroll
+    for (int off = 16; off >= 1; off >>= 1) mg[j] = fmaxf(mg[j], __shfl_xor_sync(0xffffffffu, mg[j], off));
+#pragma unroll
+  for (int k = 0; k < PER; ++k) o[k] = 0.f;
+  for (int64_t k0 = 0; k0 < count; k0 += 32) {
+    float w[QC];
+    if (k0 + lane < count) {
+      const float* pc = ptr(c0 + (k0 + lane) * stride);
+#pragma unroll
+      for (int j = 0; j < QC; ++j) {
+        w[j] = fast_exp2(__ldcg(pc + QC * D + j) - mg[j]);
+        lg[j] += __ldcg(pc + QC * D + QC + j) * w[j];
+      }
+    } else {
+#pragma unroll
+      for (int j = 0; j < QC; ++j) w[j] = 0.f;
+    }
+    const int nthis = (int)(count - k0 < 32 ? count - k0 : 32);
+#pragma unroll 4
+    for (int k = 0; k < nthis; ++k) {
+      const float* pc = ptr(c0 + (k0 + k) * stride);
+      float wk[QC];
+#pragma unroll
+      for (int j = 0; j < QC; ++j) wk[j] = __shfl_sync(0xffffffffu, w[j], k);
+#pragma unroll
+      for (int q = 0; q < PER; ++q) o[q] = fmaf(__ldcg(pc + lane + 32 * q), wk[(32 * q) / D], o[q]);
+    }
+  }
+#pragma unroll
+  for (int j = 0; j < QC; ++j)
+#pragma unroll
+    for (int off = 16; off >= 1; off >>= 1) lg[j] += __shfl_xor_sync(0xffffffffu, lg[j], off);
 }
 
 template <typename T, int D, int QC>
@@ -358,23 +414,29 @@ __global__ void __launch_bounds__(Limits<T, D, QC>::THREADS, 1)
     const unsigned char* vbase = kbase + (size_t)kTT * p.row_bytes;
     const int nvalid = h.nvalid;
 
-    // scores of this row group's tokens for the QC heads
+    // scores of this row group's tokens for the QC heads (packed pairs:
+    // even and odd elements accumulate separately, summed at the end)
     float s[TPR][QC];
 #pragma unroll
     for (int i = 0; i < TPR; ++i) {
       const int t = rg + i * NRG;
+      float2 sp[QC];
 #pragma unroll
-      for (int j = 0; j < QC; ++j) s[i][j] = 0.f;
+      for (int j = 0; j < QC; ++j) sp[j] = make_float2(0.f, 0.f);
       const unsigned char* kr = kbase + (size_t)t * p.row_bytes;
 #pragma unroll
       for (int c = 0; c < NCH; ++c) {
         float kf[VEC];
         Chunk<T>::cvt(lds128(kr + (size_t)(c * R + li) * 16), kf);
 #pragma unroll
-        for (int j = 0; j < QC; ++j)
+        for (int v = 0; v < VEC; v += 2)
 #pragma unroll
-          for (int v = 0; v < VEC; ++v) s[i][j] = fmaf(qf[j][c * VEC + v], kf[v], s[i][j]);
+          for (int j = 0; j < QC; ++j)  // independent chains back to back
+            sp[j] = fma2(make_float2(qf[j][c * VEC + v], qf[j][c * VEC + v + 1]),
+                         make_float2(kf[v], kf[v + 1]), sp[j]);
       }
+#pragma unroll
+      for (int j = 0; j < QC; ++j) s[i][j] = sp[j].x + sp[j].y;
     }
 #pragma unroll
     for (int off = R / 2; off >= 1; off >>= 1)
@@ -383,40 +445,65 @@ __global__ void __launch_bounds__(Limits<T, D, QC>::THREADS, 1)
 #pragma unroll
         for (int j = 0; j < QC; ++j) s[i][j] += __shfl_xor_sync(0xffffffffu, s[i][j], off);
 
-    // online softmax update (one rescale per stage)
+    // Online softmax with a lazy reference max: m[j] only moves when the
+    // stage's max exceeds it by more than 2^8 (then acc and l are rescaled),
+    // so weights stay below 2^8 and the usual stage rescales nothing.  Any
+    // reference gives the same result: out = acc / l and lse = m + log2(l)
+    // are taken against the same m.
+    float mt[QC];
+    bool need[QC], need_any = false;
 #pragma unroll
     for (int j = 0; j < QC; ++j) {
-      float mx = m[j];
+      mt[j] = kNegBig;
 #pragma unroll
       for (int i = 0; i < TPR; ++i)
-        if (rg + i * NRG < nvalid) mx = fmaxf(mx, s[i][j]);
-      const float corr = fast_exp2(m[j] - mx);
-      m[j] = mx;
-      float lsum = l[j] * corr;
+        if (rg + i * NRG < nvalid) mt[j] = fmaxf(mt[j], s[i][j]);
+      need[j] = mt[j] > m[j] + 8.f;
+      need_any |= need[j];
+    }
+    if (__any_sync(0xffffffffu, need_any)) {  // one vote for all heads
 #pragma unroll
-      for (int e = 0; e < EPL; ++e) acc[j][e] *= corr;
+      for (int j = 0; j < QC; ++j) {
+        const float corr = need[j] ? fast_exp2(m[j] - mt[j]) : 1.f;  // 0 on the first stage
+#pragma unroll
+        for (int e = 0; e < EPL; ++e) acc[j][e] *= corr;
+        l[j] *= corr;
+        if (need[j]) m[j] = mt[j];
+      }
+    }
+#pragma unroll
+    for (int j = 0; j < QC; ++j) {
+      float lsum = 0.f;
 #pragma unroll
       for (int i = 0; i < TPR; ++i) {
-        const float pv = (rg + i * NRG < nvalid) ? fast_exp2(s[i][j] - mx) : 0.f;
+        const float pv = (rg + i * NRG < nvalid) ? fast_exp2(s[i][j] - m[j]) : 0.f;
         s[i][j] = pv;
         lsum += pv;
       }
-      l[j] = lsum;
+      l[j] += lsum;
     }
+    // P V, branch-free: a token past nvalid reads the last valid row (finite
+    // data) with weight 0, so the V loads can be issued ahead of the softmax
 #pragma unroll
     for (int i = 0; i < TPR; ++i) {
       const int t = rg + i * NRG;
-      if (t < nvalid) {
-        const unsigned char* vr = vbase + (size_t)t * p.row_bytes;
+      {
+        const unsigned char* vr = vbase + (size_t)(t < nvalid ? t : nvalid - 1) * p.row_bytes;
 #pragma unroll
         for (int c = 0; c < NCH; ++c) {
           float vf[VEC];
           Chunk<T>::cvt(lds128(vr + (size_t)(c * R + li) * 16), vf);
 #pragma unroll
-          for (int j = 0; j < QC; ++j)
+          for (int j = 0; j < QC; ++j) {
+            const float2 pp = make_float2(s[i][j], s[i][j]);
 #pragma unroll
-            for (int v = 0; v < VEC; ++v)
-              acc[j][c * VEC + v] = fmaf(s[i][j], vf[v], acc[j][c * VEC + v]);
+            for (int v = 0; v < VEC; v += 2) {
+              const float2 a = fma2(pp, make_float2(vf[v], vf[v + 1]),
+                                    make_float2(acc[j][c * VEC + v], acc[j][c * VEC + v + 1]));
+              acc[j][c * VEC + v] = a.x;
+              acc[j][c * VEC + v + 1] = a.y;
+            }
+          }
         }
       }
     }
@@ -467,6 +554,12 @@ __global__ void __launch_bounds__(Limits<T, D, QC>::THREADS, 1)
         }
       }
     } else {
+      // Piece of a sequence split over CTAs first..last: publish the partial
+      // state; the last arriver merges.  Up to kGroup pieces merge in one
+      // step.  Longer sequences merge in two levels so no single warp reads
+      // every piece at the kernel's tail: the last arriver of each run of
+      // kGroup consecutive pieces folds them into the run's first slot, and
+      // the last run to finish merges the run results.
       const int ord = seg_count == 0 ? 0 : 1;
       const int64_t pstride = (int64_t)QC * (D + 2);
       float* mine = p.partials + ((cta * 2 + ord) * NS + slot) * pstride;
@@ -483,41 +576,51 @@ __global__ void __launch_bounds__(Limits<T, D, QC>::THREADS, 1)
           }
         }
       }
-      __threadfence();
-      __syncwarp();
-      int old = 0;
-      if (lane == 0) old = atomicAdd(&p.counters[((int64_t)gc * p.B + b) * NS + slot], 1);
-      old = __shfl_sync(0xffffffffu, old, 0);
       const int64_t first = cta_of(h.seq_t0, T_all, p.N);
       const int64_t last = cta_of(h.seq_t1 - 1, T_all, p.N);
-      if (old == (int)(last - first)) {
-        // this warp finished the sequence last: merge every piece of it
+      const int64_t npieces = last - first + 1;
+      // A CTA's first segment sits in partial slot 0, a later one in slot 1:
+      // only the first CTA of a sequence can hold it as a later segment.
+      const bool first_late = cta_lo(first, T_all, p.N) < h.seq_t0;
+      auto piece = [&](int64_t c) -> float* {
+        const int o2 = (c == first && first_late) ? 1 : 0;
+        return p.partials + ((c * 2 + o2) * NS + slot) * pstride;
+      };
+      auto arrive = [&](int32_t* counter) -> int {
         __threadfence();
-        float mg[QC], lg[QC];
+        __syncwarp();
+        int old = 0;
+        if (lane == 0) old = atomicAdd(counter, 1);
+        return __shfl_sync(0xffffffffu, old, 0);
+      };
+      constexpr int PER = QC * D / 32;
+      float o[PER], mg[QC], lg[QC];
+      int64_t n_top = npieces, top_stride = 1;
+      bool go = true;
+      if (npieces > kGroup && p.grp_counters) {
+        const int64_t g0 = first + ((cta - first) / kGroup) * kGroup;
+        const int64_t g1 = g0 + kGroup - 1 < last ? g0 + kGroup - 1 : last;
+        const int o2 = (g0 == first && first_late) ? 1 : 0;
+        go = arrive(&p.grp_counters[(g0 * 2 + o2) * NS + slot]) == (int)(g1 - g0);
+        if (go) {
+          __threadfence();
+          merge_pieces<QC, D>(piece, g0, 1, g1 - g0 + 1, lane, o, mg, lg);
+          float* dst = piece(g0);  // read above; now holds the run's merged state
 #pragma unroll
-        for (int j = 0; j < QC; ++j) { mg[j] = kNegBig; lg[j] = 0.f; }
-        for (int64_t c = first; c <= last; ++c) {
-          const int o2 = cta_lo(c, T_all, p.N) >= h.seq_t0 ? 0 : 1;
-          const float* pc = p.partials + ((c * 2 + o2) * NS + slot) * pstride;
+          for (int k = 0; k < PER; ++k) dst[lane + 32 * k] = o[k];
 #pragma unroll
-          for (int j = 0; j < QC; ++j) mg[j] = fmaxf(mg[j], __ldcg(pc + QC * D + j));
+          for (int j = 0; j < QC; ++j)
+            if (lane == j) {
+              dst[QC * D + j] = mg[j];
+              dst[QC * D + QC + j] = lg[j];
+            }
         }
-        constexpr int PER = QC * D / 32;
-        float o[PER];
-#pragma unroll
-        for (int k = 0; k < PER; ++k) o[k] = 0.f;
-        for (int64_t c = first; c <= last; ++c) {
-          const int o2 = cta_lo(c, T_all, p.N) >= h.seq_t0 ? 0 : 1;
-          const float* pc = p.partials + ((c * 2 + o2) * NS + slot) * pstride;
-          float w[QC];
-#pragma unroll
-          for (int j = 0; j < QC; ++j) {
-            w[j] = fast_exp2(__ldcg(pc + QC * D + j) - mg[j]);
-            lg[j] += __ldcg(pc + QC * D + QC + j) * w[j];
-          }
-#pragma unroll
-          for (int k = 0; k < PER; ++k) o[k] += __ldcg(pc + lane + 32 * k) * w[(32 * k) / D];
-        }
+        n_top = (npieces + kGroup - 1) / kGroup;
+        top_stride = kGroup;
+      }
+      if (go && arrive(&p.counters[((int64_t)gc * p.B + b) * NS + slot]) == (int)(n_top - 1)) {
+        __threadfence();
+        merge_pieces<QC, D>(piece, first, top_stride, n_top, lane, o, mg, lg);
 #pragma unroll
         for (int k = 0; k < PER; ++k) {
           const int j = (32 * k) / D;

@@ -146,24 +146,6 @@ __device__ __forceinline__ void split_pair(float a, float b, uint32_t& hi, uint3
   lo = 0;
 }
 
-// Packed fp32 pair arithmetic (sm_100 add/fma .f32x2: one issue slot for two
-// lanes of work).
-__device__ __forceinline__ float2 add2(float2 a, float2 b) {
-  float2 r;
-  asm("{.reg .b64 pa, pb, pd;\n\tmov.b64 pa, {%2, %3};\n\tmov.b64 pb, {%4, %5};\n\t"
-      "add.rn.ftz.f32x2 pd, pa, pb;\n\tmov.b64 {%0, %1}, pd;}"
-      : "=f"(r.x), "=f"(r.y) : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
-  return r;
-}
-__device__ __forceinline__ float2 fma2(float2 a, float2 b, float2 c) {
-  float2 r;
-  asm("{.reg .b64 pa, pb, pc, pd;\n\tmov.b64 pa, {%2, %3};\n\tmov.b64 pb, {%4, %5};\n\t"
-      "mov.b64 pc, {%6, %7};\n\tfma.rn.ftz.f32x2 pd, pa, pb, pc;\n\tmov.b64 {%0, %1}, pd;}"
-      : "=f"(r.x), "=f"(r.y)
-      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y), "f"(c.x), "f"(c.y));
-  return r;
-}
-
 // Softmax weights (p0, p1) of two adjacent keys -> the MMA operand pair(s).
 // bf16: hi = the fp32 bits truncated to bf16, lo = the remainder p - hi
 // (exact in fp32) truncated to bf16; hi + lo carries p to 2^-16 relative,

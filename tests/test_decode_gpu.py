@@ -105,6 +105,25 @@ def test_lse_output():
             assert abs(lse[b, h] - want) < 1e-3
 
 
+@pytest.mark.parametrize("num_splits", [0, 40])
+def test_long_sequences_two_level_merge(num_splits):
+    """Two long GQA sequences spread over every SM (automatic splitting) or
+    over 40 CTAs each: a sequence spans more than 8 CTAs, so its pieces merge
+    in runs of 8 and then across runs; out and lse both checked."""
+    q, k, v, bt, ctx = case(16, 2, 32, 8, 128, 16, [9000, 3001], "bfloat16")
+    scale = 0.088
+    out, lse = abi_decode(q, k, v, bt, ctx, scale, "bfloat16", want_lse=True,
+                          num_splits=num_splits)
+    assert max_abs(out, orc.decode(q, k, v, bt, ctx, scale)) <= 2e-3
+    for b in range(2):
+        n = int(ctx[b])
+        ks = k[bt[b, :(n + 15) // 16]].reshape(-1, 8, 128)[:n].astype(np.float64)
+        for h in (0, 5, 31):
+            s = scale * ks[:, h // 4] @ q[b, h].astype(np.float64)
+            want = s.max() + np.log(np.exp(s - s.max()).sum())
+            assert abs(lse[b, h] - want) < 1e-3
+
+
 def test_hip_selftest_fixture():
     """The reference's own HIP self-test (mt19937(7) inputs, tolerance 3e-4,
     rocm/hip/paged_attn_v1_hip.cpp:151-198) run on the B200 kernel."""
