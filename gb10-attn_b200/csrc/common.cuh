@@ -148,16 +148,19 @@ constexpr uint64_t kWaitLimitNs = 1000ull * 1000ull * 1000ull;  // 1 s
 
 // `abort_flag` (global, per launch) makes every CTA give up as soon as one
 // wait anywhere in the grid has timed out, so a failure costs ~1 s in total.
+// The flag holds `abort_tag` once a wait has given up; a launch that does not
+// zero the flag first passes a tag of its own, so a stale value left by an
+// earlier launch reads as "no abort".
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity,
-                                          int32_t* abort_flag = nullptr) {
+                                          int32_t* abort_flag = nullptr, int32_t abort_tag = 1) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = globaltimer_ns();
   for (uint32_t it = 1;; ++it) {
     if (mbar_try_wait_sleep(bar, parity, 100000u)) return true;
     if ((it & 7) == 0) {
-      if (abort_flag && *reinterpret_cast<volatile int32_t*>(abort_flag) != 0) return false;
+      if (abort_flag && *reinterpret_cast<volatile int32_t*>(abort_flag) == abort_tag) return false;
       if (globaltimer_ns() - t0 > kWaitLimitNs) {
-        if (abort_flag) atomicExch(abort_flag, 1);
+        if (abort_flag) atomicExch(abort_flag, abort_tag);
         return false;
       }
     }

@@ -4,6 +4,8 @@
 // (pa_paged_attention, _v2, _v3, pa_choose_num_splits,
 // pa_decode_workspace_size, pa_merge_states, pa_validate_block_tables).
 #include <algorithm>
+#include <atomic>
+#include <chrono>
 #include <limits>
 #include <mutex>
 #include <vector>
@@ -56,6 +58,7 @@ constexpr uint32_t kRingBudget = 200 * 1024;  // bytes of stages per CTA
 struct Config {
   int QC, G, NS, NGC, nstage, threads, N;
   int64_t n_grp;  // run counters for two-level merges (0: single-level merges)
+  bool fused;     // plan built by each CTA (no plan kernel)
   uint32_t row_bytes;
   size_t smem;
   const void* kernel;
@@ -64,24 +67,34 @@ struct Config {
 };
 
 static size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
-constexpr int64_t kMaxRunCounters = 16384;
+constexpr int64_t kMaxRunCounters = int64_t(1) << 20;  // 8 MB of workspace at most
+
+// Launch epoch: tags the merge counters and the abort flag of one launch, so
+// no kernel has to zero them.  40 bits, never 0; starts from the clock so two
+// processes sharing a workspace layout do not replay each other's tags.
+static void next_epoch(unsigned long long* epoch, int32_t* abort_tag) {
+  static std::atomic<unsigned long long> ctr{
+      (unsigned long long)std::chrono::steady_clock::now().time_since_epoch().count() * 2654435761ull};
+  unsigned long long e = ctr.fetch_add(1) & ((1ull << (64 - kCountBits)) - 1);
+  if (e == 0) e = 1;
+  *epoch = e;
+  *abort_tag = (int32_t)(1 + e % 0x7ffffffeull);
+}
 
 struct PlanParams {
   const int32_t* context_lens;
   int32_t* tile_off;   // [B + 1]
   int32_t* cta_seq;    // [N]
-  int32_t* counters;   // [NGC * B * NS + N * 2 * NS]
-  int32_t* abort_flag;
   float* out;          // rows of empty sequences are filled with empty_fill
   float* lse;
   int32_t* dev_status;
-  int64_t B, H, D, max_ctx, n_counters, qlen;
+  int64_t B, H, D, max_ctx, qlen;
   int32_t NGC, N;
   float empty_fill;
 };
 
-// One CTA: tile counts -> exclusive scan -> tile_off; zero the merge
-// counters; the sequence holding each CTA's first tile; NaN rows for empty
+// One CTA: tile counts -> exclusive scan -> tile_off; the sequence holding
+// each CTA's first tile; NaN rows for empty
 // sequences (the reference's v3 yields NaN there, paged_attn_v3.cu:160-165).
 __global__ void __launch_bounds__(kPlanThreads) plan_kernel(const __grid_constant__ PlanParams pp) {
   // Launched with programmatic stream serialisation: let the decode kernel
@@ -137,11 +150,7 @@ __global__ void __launch_bounds__(kPlanThreads) plan_kernel(const __grid_constan
     if (tid == kPlanThreads - 1) carry_s = carry + warp_tot[kPlanThreads / 32 - 1];
     __syncthreads();
   }
-  if (tid == 0) {
-    pp.tile_off[pp.B] = carry_s;
-    *pp.abort_flag = 0;
-  }
-  for (int64_t i = tid; i < pp.n_counters; i += kPlanThreads) pp.counters[i] = 0;
+  if (tid == 0) pp.tile_off[pp.B] = carry_s;
   __syncthreads();
   const int64_t Tpg = carry_s;
   const int64_t T_all = Tpg * pp.NGC;
@@ -297,19 +306,23 @@ static int configure(const DecodeArgs& a, Config* c) {
   if (N > (int64_t(1) << 24) || t_upper > (int64_t(1) << 36)) return PA_ERR_TOO_LARGE;
   c->N = (int)N;
 
+  // Small batches: every CTA builds the plan in shared memory (no plan
+  // kernel, tables beside the stage headers).
+  c->fused = rows <= kFusedRows;
+  if (c->fused) c->smem += sizeof(int32_t) * (size_t)(2 * rows + 1 + 33);
+
   size_t off = 0;
   c->off_abort = off;
   off = align256(off + sizeof(int32_t));
   c->off_tile = off;
-  off = align256(off + sizeof(int32_t) * (size_t)(rows + 1));
+  if (!c->fused) off = align256(off + sizeof(int32_t) * (size_t)(rows + 1));
   c->off_cta = off;
-  off = align256(off + sizeof(int32_t) * (size_t)N);
+  if (!c->fused) off = align256(off + sizeof(int32_t) * (size_t)N);
   c->off_cnt = off;
-  // per-(g-chunk, row, slot) merge counters, then per-(CTA, slot) run counters
-  // for two-level merges -- only while the plan kernel zeroes them in a few
-  // passes (automatic splitting: N = SMs x resident CTAs)
+  // epoch-tagged merge counters per (g-chunk, row, slot), then per (CTA,
+  // slot) run counters for two-level merges (bounded workspace)
   c->n_grp = (N * 2 * c->NS <= kMaxRunCounters) ? N * 2 * c->NS : 0;
-  off = align256(off + sizeof(int32_t) * ((size_t)c->NGC * rows * c->NS + (size_t)c->n_grp));
+  off = align256(off + sizeof(unsigned long long) * ((size_t)c->NGC * rows * c->NS + (size_t)c->n_grp));
   c->off_part = off;
   off = align256(off + sizeof(float) * (size_t)N * 2 * c->NS * QC * (a.D + 2));
   c->total = off;
@@ -336,8 +349,6 @@ int launch(const DecodeArgs& a, void* ws, size_t ws_bytes, cudaStream_t stream) 
   pp.context_lens = a.context_lens;
   pp.tile_off = reinterpret_cast<int32_t*>(w + c.off_tile);
   pp.cta_seq = reinterpret_cast<int32_t*>(w + c.off_cta);
-  pp.counters = reinterpret_cast<int32_t*>(w + c.off_cnt);
-  pp.abort_flag = reinterpret_cast<int32_t*>(w + c.off_abort);
   pp.out = a.out;
   pp.lse = a.lse;
   pp.dev_status = a.dev_status;
@@ -345,7 +356,6 @@ int launch(const DecodeArgs& a, void* ws, size_t ws_bytes, cudaStream_t stream) 
   pp.H = a.H;
   pp.D = a.D;
   pp.max_ctx = a.MB * a.BS;
-  pp.n_counters = (int64_t)c.NGC * pp.B * c.NS + c.n_grp;
   pp.qlen = a.qlen;
   pp.NGC = c.NGC;
   pp.N = c.N;
@@ -353,14 +363,17 @@ int launch(const DecodeArgs& a, void* ws, size_t ws_bytes, cudaStream_t stream) 
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = 1;
-  cudaLaunchConfig_t pcfg = {};
-  pcfg.gridDim = dim3(1);
-  pcfg.blockDim = dim3(kPlanThreads);
-  pcfg.stream = stream;
-  pcfg.attrs = attr;
-  pcfg.numAttrs = 1;
-  cudaError_t e = cudaLaunchKernelEx(&pcfg, plan_kernel, pp);
-  if (e != cudaSuccess) return cuda_status(e);
+  cudaError_t e;
+  if (!c.fused) {
+    cudaLaunchConfig_t pcfg = {};
+    pcfg.gridDim = dim3(1);
+    pcfg.blockDim = dim3(kPlanThreads);
+    pcfg.stream = stream;
+    pcfg.attrs = attr;
+    pcfg.numAttrs = 1;
+    e = cudaLaunchKernelEx(&pcfg, plan_kernel, pp);
+    if (e != cudaSuccess) return cuda_status(e);
+  }
 
   Params p;
   p.out = a.out;
@@ -371,11 +384,13 @@ int launch(const DecodeArgs& a, void* ws, size_t ws_bytes, cudaStream_t stream) 
   p.block_tables = a.block_tables;
   p.context_lens = a.context_lens;
   p.dev_status = a.dev_status;
-  p.tile_off = pp.tile_off;
-  p.cta_seq = pp.cta_seq;
-  p.counters = pp.counters;
-  p.grp_counters = c.n_grp ? pp.counters + (int64_t)c.NGC * pp.B * c.NS : nullptr;
-  p.abort_flag = pp.abort_flag;
+  p.tile_off = c.fused ? nullptr : pp.tile_off;
+  p.cta_seq = c.fused ? nullptr : pp.cta_seq;
+  p.counters = reinterpret_cast<unsigned long long*>(w + c.off_cnt);
+  p.grp_counters = c.n_grp ? p.counters + (int64_t)c.NGC * pp.B * c.NS : nullptr;
+  p.abort_flag = reinterpret_cast<int32_t*>(w + c.off_abort);
+  next_epoch(&p.epoch, &p.abort_tag);
+  p.empty_fill = a.empty_fill;
   p.partials = reinterpret_cast<float*>(w + c.off_part);
   p.B = a.B * a.qlen;
   p.qlen = a.qlen;

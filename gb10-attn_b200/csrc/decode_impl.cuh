@@ -38,6 +38,8 @@ namespace decode {
 
 constexpr int kTT = 16;            // tokens per pipeline stage
 constexpr int kGroup = 8;          // pieces merged per step of a split sequence
+constexpr int kFusedRows = 1024;   // rows up to which each CTA plans for itself
+constexpr int kCountBits = 24;     // arrival count bits of an epoch-tagged counter
 constexpr float kNegBig = -3.0e38f;  // the reference's "minus infinity" (paged_attn_v3.cu:20)
 
 struct Params {
@@ -49,11 +51,18 @@ struct Params {
   const int32_t* block_tables;   // [B, MB]
   const int32_t* context_lens;   // [B]
   int32_t* dev_status;           // nullable
+  // Plan tables from the plan kernel, or null: then every CTA builds them in
+  // shared memory from context_lens (B <= kFusedRows).
   const int32_t* tile_off;       // [B + 1] tiles before sequence b (per g-chunk)
   const int32_t* cta_seq;        // [N] sequence holding each CTA's first tile
-  int32_t* counters;             // [NGC * B * NS] merge arrival counters
-  int32_t* grp_counters;         // [N * 2 * NS] arrivals per run of kGroup pieces, or null
-  int32_t* abort_flag;           // set when any pipeline wait times out
+  // Merge arrival counters, tagged with the launch's epoch in the high bits
+  // so no launch has to zero them: a value from an earlier launch reads as 0.
+  unsigned long long* counters;      // [NGC * B * NS]
+  unsigned long long* grp_counters;  // [N * 2 * NS] arrivals per run of kGroup pieces, or null
+  unsigned long long epoch;          // this launch's tag (nonzero, < 2^40)
+  int32_t* abort_flag;           // holds abort_tag once any pipeline wait timed out
+  int32_t abort_tag;
+  float empty_fill;              // rows of empty sequences (fused plan)
   float* partials;               // [N * 2 * NS * QC * (D + 2)]
   int64_t B, H, HKV, NB, MB, BS;
   // Query rows per block-table row: 1 for decode.  For causal prefill row
@@ -98,8 +107,8 @@ struct Geo {
 //    launched at 96 registers (20 warps, 5 per SM sub-partition) = 61440; after
 //    the split 128 x 40 + 512 x 104 = 58368.
 //  * kWs8 (larger S): warpgroup 0 producer, warpgroups 1-2 = 8 consumer warps.
-//    384 threads x 168 registers = 64512; after the split 128 x 48 + 256 x 224
-//    = 63488.
+//    384 threads x 168 registers = 64512; after the split 128 x 56 + 256 x 224
+//    = 64512.
 // setmaxnreg.inc draws on the registers the CTA was launched with, so each
 // split stays inside its launch total (checked below).
 enum CtaKind { kLight = 0, kWs16 = 1, kWs8 = 2 };
@@ -112,10 +121,10 @@ struct Limits {
   static constexpr bool WS = KIND != kLight;
   static constexpr int MAXW = KIND == kWs8 ? 8 : 16;
   static constexpr int THREADS = KIND == kWs8 ? 384 : (KIND == kWs16 ? 640 : 544);
-  static constexpr int PROD_REGS = KIND == kWs8 ? 48 : 40;
+  static constexpr int PROD_REGS = KIND == kWs8 ? 56 : 40;
   static constexpr int CONS_REGS = KIND == kWs8 ? 224 : 104;
 };
-static_assert(128 * 48 + 256 * 224 <= 384 * 168, "kWs8 register split exceeds launch");
+static_assert(128 * 56 + 256 * 224 <= 384 * 168, "kWs8 register split exceeds launch");
 static_assert(128 * 40 + 512 * 104 <= 640 * 96, "kWs16 register split exceeds launch");
 
 __host__ __device__ __forceinline__ int64_t cta_lo(int64_t c, int64_t T_all, int64_t N) {
@@ -124,6 +133,83 @@ __host__ __device__ __forceinline__ int64_t cta_lo(int64_t c, int64_t T_all, int
 // CTA whose range holds global tile t < T_all: the largest c with cta_lo(c) <= t.
 __host__ __device__ __forceinline__ int64_t cta_of(int64_t t, int64_t T_all, int64_t N) {
   return T_all >= N ? ((t + 1) * N - 1) / T_all : t;
+}
+
+// One arrival on an epoch-tagged counter (value = epoch << kCountBits |
+// count); returns the arrivals of this launch before it.  A value left by an
+// earlier launch (another epoch) counts as zero, so counters are never reset.
+__device__ __forceinline__ int epoch_arrive(unsigned long long* counter, unsigned long long epoch) {
+  unsigned long long v = *reinterpret_cast<volatile unsigned long long*>(counter);
+  for (int it = 0; it < (1 << 20); ++it) {  // lock-free: one CAS wins per round
+    const bool same = (v >> kCountBits) == epoch;
+    const unsigned long long nv = same ? v + 1 : ((epoch << kCountBits) | 1ull);
+    const unsigned long long prev = atomicCAS(counter, v, nv);
+    if (prev == v) return same ? (int)(v & ((1ull << kCountBits) - 1)) : 0;
+    v = prev;
+  }
+  return -1;  // never settled: no merge from this arrival
+}
+
+// The plan of one launch built by every CTA in shared memory (B <= kFusedRows
+// rows; scratch = 33 words): tile_off_s[b] = tiles of rows 0..b-1, ntok_s[b] = keys row b reads
+// (the plan kernel's rule: a query row s of qlen sees context - qlen + s + 1
+// keys, clamped to the block table).  CTA b % gridDim fills the output rows of
+// empty sequences (the reference's v3 yields NaN there, paged_attn_v3.cu:160-165).
+template <int D>
+__device__ __forceinline__ void fused_plan(const Params& p, int32_t* tile_off_s, int32_t* ntok_s,
+                                           int32_t* scratch) {
+  int32_t* warp_tot = scratch;     // [32]
+  int32_t& carry_s = scratch[32];
+  const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5, nw = blockDim.x >> 5;
+  const int64_t max_ctx = p.MB * p.BS;
+  if (tid == 0) carry_s = 0;
+  __syncthreads();
+  for (int64_t base = 0; base < p.B; base += blockDim.x) {
+    const int64_t b = base + tid;
+    int32_t tiles = 0;
+    if (b < p.B) {
+      const int64_t sq = b / p.qlen;
+      const int64_t c = p.context_lens[sq];
+      if (c > max_ctx && b == sq * p.qlen && blockIdx.x == 0) report(p.dev_status, PA_DEVERR_CONTEXT);
+      int64_t n = c - p.qlen + (b - sq * p.qlen) + 1;
+      if (n > max_ctx) n = max_ctx;
+      if (n <= 0) {
+        n = 0;
+        if (b % gridDim.x == blockIdx.x) {
+          for (int64_t i = 0; i < p.H * D; ++i) p.out[b * p.H * D + i] = p.empty_fill;
+          if (p.lse)
+            for (int64_t h = 0; h < p.H; ++h) p.lse[b * p.H + h] = -INFINITY;
+        }
+      }
+      ntok_s[b] = (int32_t)n;
+      tiles = (int32_t)((n + kTT - 1) / kTT);
+    }
+    int32_t x = tiles;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int32_t y = __shfl_up_sync(0xffffffffu, x, o);
+      if (lane >= o) x += y;
+    }
+    if (lane == 31) warp_tot[wid] = x;
+    __syncthreads();
+    if (wid == 0) {
+      int32_t w = lane < nw ? warp_tot[lane] : 0;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int32_t y = __shfl_up_sync(0xffffffffu, w, o);
+        if (lane >= o) w += y;
+      }
+      if (lane < nw) warp_tot[lane] = w;  // inclusive over warps
+    }
+    __syncthreads();
+    const int32_t carry = carry_s;
+    if (b < p.B) tile_off_s[b] = carry + (wid ? warp_tot[wid - 1] : 0) + x - tiles;
+    __syncthreads();
+    if (tid == 0) carry_s = carry + warp_tot[nw - 1];
+    __syncthreads();
+  }
+  if (tid == 0) tile_off_s[p.B] = carry_s;
+  __syncthreads();
 }
 
 // Log-sum-exp merge of the partial states at ptr(c0), ptr(c0 + stride), ...
@@ -206,13 +292,27 @@ __global__ void __launch_bounds__(Limits<T, D, QC>::THREADS, 1)
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   __syncthreads();
-  // Everything above overlaps the plan kernel; its tables are read below.
-  // The next call's plan kernel may launch now: it waits for this grid to
-  // complete before it touches memory.
+  // Everything above overlaps the previous kernel on the stream (the plan
+  // kernel, or the previous call); its results are read below.  The next
+  // kernel may launch now: it waits for this grid to complete before it
+  // touches memory.
   pdl_wait();
   pdl_trigger();
 
-  const int64_t Tpg = p.tile_off[p.B];  // tiles per g-chunk
+  // Plan tables: the plan kernel's (global) or, for small batches, built here
+  // by the whole CTA in shared memory -- no plan kernel on the stream and no
+  // global round trips when the producer moves to the next sequence.
+  const int32_t* tile_off = p.tile_off;
+  const int32_t* ntok_s = nullptr;
+  if (tile_off == nullptr) {
+    int32_t* to_s = reinterpret_cast<int32_t*>(hdr + nstage);
+    int32_t* nt_s = to_s + p.B + 1;
+    fused_plan<D>(p, to_s, nt_s, nt_s + p.B);
+    tile_off = to_s;
+    ntok_s = nt_s;
+  }
+
+  const int64_t Tpg = tile_off[p.B];  // tiles per g-chunk
   const int64_t T_all = Tpg * p.NGC;
   const int64_t cta = blockIdx.x;
   const int64_t lo = cta_lo(cta, T_all, p.N), hi = cta_lo(cta + 1, T_all, p.N);
@@ -237,10 +337,22 @@ __global__ void __launch_bounds__(Limits<T, D, QC>::THREADS, 1)
       int64_t gt = lo;
       int gc = (int)(lo / Tpg);
       int64_t r = lo - (int64_t)gc * Tpg;
-      int b = p.cta_seq[cta];
-      int64_t s0 = p.tile_off[b], s1 = p.tile_off[b + 1];
+      int b;
+      if (p.cta_seq) {
+        b = p.cta_seq[cta];
+      } else {  // upper_bound(tile_off[0..B], r) - 1
+        int64_t a = 0, z = p.B + 1;
+        while (a < z) {
+          const int64_t mid = (a + z) >> 1;
+          if (tile_off[mid] <= r) a = mid + 1;
+          else z = mid;
+        }
+        b = (int)(a - 1);
+      }
+      int64_t s0 = tile_off[b], s1 = tile_off[b + 1];
       const int64_t max_ctx = p.MB * p.BS;
       auto seq_len = [&](int bb) -> int64_t {
+        if (ntok_s) return ntok_s[bb];
         const int64_t sq = bb / p.qlen;
         int64_t n = (int64_t)p.context_lens[sq] - p.qlen + (bb - sq * p.qlen) + 1;
         if (n > max_ctx) n = max_ctx;
@@ -273,7 +385,7 @@ __global__ void __launch_bounds__(Limits<T, D, QC>::THREADS, 1)
           }
           win_next = bt_load(win_base + 32 + lane);
         }
-        if (!mbar_wait(&empty[stage], phase ^ 1, p.abort_flag)) { ok = false; break; }
+        if (!mbar_wait(&empty[stage], phase ^ 1, p.abort_flag, p.abort_tag)) { ok = false; break; }
 
         const int row = lane & 15, kv = lane >> 4;
         const int64_t tok = tok0 + row;
@@ -328,16 +440,16 @@ __global__ void __launch_bounds__(Limits<T, D, QC>::THREADS, 1)
         if (gt < hi && r == s1) {
           if (r == Tpg) { ++gc; r = 0; b = 0; }
           else ++b;
-          while (p.tile_off[b + 1] == p.tile_off[b]) ++b;  // skip empty sequences
-          s0 = p.tile_off[b];
-          s1 = p.tile_off[b + 1];
+          while (tile_off[b + 1] == tile_off[b]) ++b;  // skip empty sequences
+          s0 = tile_off[b];
+          s1 = tile_off[b + 1];
           n_tok = seq_len(b);
           bt = p.block_tables + (int64_t)(b / p.qlen) * p.MB;
           win_base = -1;
         }
       }
     }
-    if (ok && mbar_wait(&empty[stage], phase ^ 1, p.abort_flag)) {
+    if (ok && mbar_wait(&empty[stage], phase ^ 1, p.abort_flag, p.abort_tag)) {
       if (lane == 0) {
         hdr[stage].flags = kEnd;
         mbar_arrive(&full[stage]);
@@ -377,7 +489,7 @@ __global__ void __launch_bounds__(Limits<T, D, QC>::THREADS, 1)
   int64_t head0 = 0;
 
   while (true) {
-    if (!mbar_wait(&full[stage], phase, p.abort_flag)) {
+    if (!mbar_wait(&full[stage], phase, p.abort_flag, p.abort_tag)) {
       if (lane == 0) report(p.dev_status, PA_DEVERR_TIMEOUT);
       break;
     }
@@ -586,11 +698,11 @@ __global__ void __launch_bounds__(Limits<T, D, QC>::THREADS, 1)
         const int o2 = (c == first && first_late) ? 1 : 0;
         return p.partials + ((c * 2 + o2) * NS + slot) * pstride;
       };
-      auto arrive = [&](int32_t* counter) -> int {
+      auto arrive = [&](unsigned long long* counter) -> int {
         __threadfence();
         __syncwarp();
         int old = 0;
-        if (lane == 0) old = atomicAdd(counter, 1);
+        if (lane == 0) old = epoch_arrive(counter, p.epoch);
         return __shfl_sync(0xffffffffu, old, 0);
       };
       constexpr int PER = QC * D / 32;
