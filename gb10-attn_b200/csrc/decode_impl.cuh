@@ -365,6 +365,8 @@ __global__ void __launch_bounds__(Limits<T, D, QC>::THREADS, 1)
       };
       int64_t win_base = -1;
       int32_t win_cur = 0, win_next = 0;
+      int nx_b = 0, nx_gc = 0;           // the next sequence of this CTA's range
+      int32_t nx_cur = 0, nx_next = 0;   // its first block-table window
       const int64_t gbytes = (int64_t)p.G * D * (int64_t)sizeof(T);
       const uint32_t qbytes = (uint32_t)(p.G * p.QPK * D * 4);
 
@@ -434,18 +436,35 @@ __global__ void __launch_bounds__(Limits<T, D, QC>::THREADS, 1)
           }
         }
 
+        // On a sequence's last tile (when the range goes on): find the next
+        // sequence, start loading its first block-table window and warm its q
+        // in L2 now, so the switch does not wait on global memory.
+        if (r + 1 == s1 && gt + 1 < hi) {
+          nx_gc = gc;
+          nx_b = b;
+          if (r + 1 == Tpg) { ++nx_gc; nx_b = 0; }
+          else ++nx_b;
+          while (tile_off[nx_b + 1] == tile_off[nx_b]) ++nx_b;  // skip empty sequences
+          const int32_t* nbt = p.block_tables + (int64_t)(nx_b / p.qlen) * p.MB;
+          nx_cur = lane < p.MB ? __ldg(nbt + lane) : 0;
+          nx_next = 32 + lane < p.MB ? __ldg(nbt + 32 + lane) : 0;
+          if (lane == 0)
+            prefetch_l2(p.q + ((int64_t)nx_b * p.H + (int64_t)nx_gc * p.G * p.QPK) * D, qbytes);
+        }
         ++gt;
         ++r;
         if (++stage == nstage) { stage = 0; phase ^= 1; }
         if (gt < hi && r == s1) {
-          if (r == Tpg) { ++gc; r = 0; b = 0; }
-          else ++b;
-          while (tile_off[b + 1] == tile_off[b]) ++b;  // skip empty sequences
+          if (r == Tpg) r = 0;
+          gc = nx_gc;
+          b = nx_b;
           s0 = tile_off[b];
           s1 = tile_off[b + 1];
           n_tok = seq_len(b);
           bt = p.block_tables + (int64_t)(b / p.qlen) * p.MB;
-          win_base = -1;
+          win_base = 0;  // the new sequence starts at its first page
+          win_cur = nx_cur;
+          win_next = nx_next;
         }
       }
     }
@@ -480,6 +499,73 @@ __global__ void __launch_bounds__(Limits<T, D, QC>::THREADS, 1)
 #pragma unroll
     for (int e = 0; e < EPL; ++e) { acc[j][e] = 0.f; qf[j][e] = 0.f; }
   }
+
+  // Arrival of a written piece of a split sequence (row pb, g-chunk pgc,
+  // first head phead0, global tiles [t0, t1)); the last arriver merges.  Up to
+  // kGroup pieces merge in one step.  Longer sequences merge in two levels so
+  // no single warp reads every piece at the kernel's tail: the last arriver of
+  // each run of kGroup consecutive pieces folds them into the run's first
+  // slot, and the last run to finish merges the run results.
+  const int64_t pstride = (int64_t)QC * (D + 2);
+  auto publish = [&](int pb, int pgc, int64_t phead0, int64_t t0, int64_t t1) {
+    const int64_t first = cta_of(t0, T_all, p.N);
+    const int64_t last = cta_of(t1 - 1, T_all, p.N);
+    const int64_t npieces = last - first + 1;
+    // A CTA's first segment sits in partial slot 0, a later one in slot 1:
+    // only the first CTA of a sequence can hold it as a later segment.
+    const bool first_late = cta_lo(first, T_all, p.N) < t0;
+    auto piece = [&](int64_t c) -> float* {
+      const int o2 = (c == first && first_late) ? 1 : 0;
+      return p.partials + ((c * 2 + o2) * NS + slot) * pstride;
+    };
+    auto arrive = [&](unsigned long long* counter) -> int {
+      __threadfence();
+      __syncwarp();
+      int old = 0;
+      if (lane == 0) old = epoch_arrive(counter, p.epoch);
+      return __shfl_sync(0xffffffffu, old, 0);
+    };
+    constexpr int PER = QC * D / 32;
+    float o[PER], mg[QC], lg[QC];
+    int64_t n_top = npieces, top_stride = 1;
+    bool go = true;
+    if (npieces > kGroup && p.grp_counters) {
+      const int64_t g0 = first + ((cta - first) / kGroup) * kGroup;
+      const int64_t g1 = g0 + kGroup - 1 < last ? g0 + kGroup - 1 : last;
+      const int o2 = (g0 == first && first_late) ? 1 : 0;
+      go = arrive(&p.grp_counters[(g0 * 2 + o2) * NS + slot]) == (int)(g1 - g0);
+      if (go) {
+        __threadfence();
+        merge_pieces<QC, D>(piece, g0, 1, g1 - g0 + 1, lane, o, mg, lg);
+        float* dst = piece(g0);  // read above; now holds the run's merged state
+#pragma unroll
+        for (int k = 0; k < PER; ++k) dst[lane + 32 * k] = o[k];
+#pragma unroll
+        for (int j = 0; j < QC; ++j)
+          if (lane == j) {
+            dst[QC * D + j] = mg[j];
+            dst[QC * D + QC + j] = lg[j];
+          }
+      }
+      n_top = (npieces + kGroup - 1) / kGroup;
+      top_stride = kGroup;
+    }
+    if (go && arrive(&p.counters[((int64_t)pgc * p.B + pb) * NS + slot]) == (int)(n_top - 1)) {
+      __threadfence();
+      merge_pieces<QC, D>(piece, first, top_stride, n_top, lane, o, mg, lg);
+#pragma unroll
+      for (int k = 0; k < PER; ++k) {
+        const int j = (32 * k) / D;
+        const int e = (lane + 32 * k) - j * D;
+        p.out[((int64_t)pb * p.H + phead0 + j) * D + e] = o[k] / lg[j];
+      }
+      if (p.lse && lane < QC) {
+#pragma unroll
+        for (int j = 0; j < QC; ++j)
+          if (lane == j) p.lse[(int64_t)pb * p.H + phead0 + j] = (mg[j] + __log2f(lg[j])) * kLn2;
+      }
+    }
+  };
 
   int stage = 0;
   uint32_t phase = 0;
@@ -666,14 +752,11 @@ __global__ void __launch_bounds__(Limits<T, D, QC>::THREADS, 1)
         }
       }
     } else {
-      // Piece of a sequence split over CTAs first..last: publish the partial
-      // state; the last arriver merges.  Up to kGroup pieces merge in one
-      // step.  Longer sequences merge in two levels so no single warp reads
-      // every piece at the kernel's tail: the last arriver of each run of
-      // kGroup consecutive pieces folds them into the run's first slot, and
-      // the last run to finish merges the run results.
+      // Piece of a sequence split over CTAs first..last: write the partial
+      // state and publish it at once (published at the kernel's end instead,
+      // the arrivals of CTAs that move on to another sequence lengthen the
+      // tail more than they stall the pipeline here).
       const int ord = seg_count == 0 ? 0 : 1;
-      const int64_t pstride = (int64_t)QC * (D + 2);
       float* mine = p.partials + ((cta * 2 + ord) * NS + slot) * pstride;
       if (rg == 0) {
 #pragma unroll
@@ -688,63 +771,7 @@ __global__ void __launch_bounds__(Limits<T, D, QC>::THREADS, 1)
           }
         }
       }
-      const int64_t first = cta_of(h.seq_t0, T_all, p.N);
-      const int64_t last = cta_of(h.seq_t1 - 1, T_all, p.N);
-      const int64_t npieces = last - first + 1;
-      // A CTA's first segment sits in partial slot 0, a later one in slot 1:
-      // only the first CTA of a sequence can hold it as a later segment.
-      const bool first_late = cta_lo(first, T_all, p.N) < h.seq_t0;
-      auto piece = [&](int64_t c) -> float* {
-        const int o2 = (c == first && first_late) ? 1 : 0;
-        return p.partials + ((c * 2 + o2) * NS + slot) * pstride;
-      };
-      auto arrive = [&](unsigned long long* counter) -> int {
-        __threadfence();
-        __syncwarp();
-        int old = 0;
-        if (lane == 0) old = epoch_arrive(counter, p.epoch);
-        return __shfl_sync(0xffffffffu, old, 0);
-      };
-      constexpr int PER = QC * D / 32;
-      float o[PER], mg[QC], lg[QC];
-      int64_t n_top = npieces, top_stride = 1;
-      bool go = true;
-      if (npieces > kGroup && p.grp_counters) {
-        const int64_t g0 = first + ((cta - first) / kGroup) * kGroup;
-        const int64_t g1 = g0 + kGroup - 1 < last ? g0 + kGroup - 1 : last;
-        const int o2 = (g0 == first && first_late) ? 1 : 0;
-        go = arrive(&p.grp_counters[(g0 * 2 + o2) * NS + slot]) == (int)(g1 - g0);
-        if (go) {
-          __threadfence();
-          merge_pieces<QC, D>(piece, g0, 1, g1 - g0 + 1, lane, o, mg, lg);
-          float* dst = piece(g0);  // read above; now holds the run's merged state
-#pragma unroll
-          for (int k = 0; k < PER; ++k) dst[lane + 32 * k] = o[k];
-#pragma unroll
-          for (int j = 0; j < QC; ++j)
-            if (lane == j) {
-              dst[QC * D + j] = mg[j];
-              dst[QC * D + QC + j] = lg[j];
-            }
-        }
-        n_top = (npieces + kGroup - 1) / kGroup;
-        top_stride = kGroup;
-      }
-      if (go && arrive(&p.counters[((int64_t)gc * p.B + b) * NS + slot]) == (int)(n_top - 1)) {
-        __threadfence();
-        merge_pieces<QC, D>(piece, first, top_stride, n_top, lane, o, mg, lg);
-#pragma unroll
-        for (int k = 0; k < PER; ++k) {
-          const int j = (32 * k) / D;
-          const int e = (lane + 32 * k) - j * D;
-          p.out[((int64_t)b * p.H + head0 + j) * D + e] = o[k] / lg[j];
-        }
-        if (p.lse && lane < QC) {
-#pragma unroll
-          for (int j = 0; j < QC; ++j)
-            if (lane == j) p.lse[(int64_t)b * p.H + head0 + j] = (mg[j] + __log2f(lg[j])) * kLn2;
-        }
-      }
+      publish(b, gc, head0, h.seq_t0, h.seq_t1);
     }
     ++seg_count;
   }
