@@ -243,11 +243,11 @@ def run_b200(args) -> None:
     e2e_val = total_bytes / (e2e_ms * 1e-3) / 1e9 if e2e_ms == e2e_ms else None
     peaks = _peaks()
     # decode-kernel roofline: bytes of one layer call / mean call time over the
-    # timed region (events on the launching stream; the call's plan kernel is
-    # included, so this is a lower bound on the kernel's own rate)
+    # timed region (events on the launching stream).  With B <= 1024 rows the
+    # plan is built inside the decode kernel, so a call is one launch.
     call_ms = t_ms / (args.steps * L)
     achieved = bytes_per_call / (call_ms * 1e-3) / 1e9
-    traffic = _profile_traffic("decode_kernel")
+    traffic = _profile_traffic("decode_kernel_config2")
     clk = clocks.summary()
 
     line = {
@@ -271,12 +271,12 @@ def run_b200(args) -> None:
                 "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                 "tokens_per_s": round(B * world * args.steps / (e2e_ms * 1e-3), 1)
                 if e2e_val else None},
-        "gpu_launches": 2 * L * args.steps,
+        "gpu_launches": (1 if B <= 1024 else 2) * L * args.steps,
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1),
                      "peak": peaks["hbm_gbs"], "unit": "GB/s",
                      "frac": round(achieved / peaks["hbm_gbs"], 4),
                      "traffic": traffic, "peak_source": peaks["src"],
-                     "kernel": "pa::decode::decode_kernel<__half,64,1> (+ plan_kernel, PDL)",
+                     "kernel": "pa::decode::decode_kernel<__half,64,1> (plan built in-kernel)",
                      "bytes_per_launch": bytes_per_call,
                      "launch_us": round(call_ms * 1e3, 2),
                      "isolated_launch_us": round(launch_ms * 1e3, 2)},
@@ -305,7 +305,7 @@ def run_config3(torch, ops, harness, dev, stream, args, peaks) -> dict:
     4 disjoint regions rotated per call (each call reads ~0.55 GB)."""
     H3, HKV3, D3, BS3, B3, NB3, REG = 32, 8, 128, 16, 8, args.pool_blocks, 4
     rng = np.random.default_rng(2026)
-    ctx = rng.integers(1024, 32769, size=B3).astype(np.int32)
+    ctx = rng.integers(1024, 32769, size=B3).astype(np.int32) * int(args.ctx_scale)
     need = [int(-(-c // BS3)) for c in ctx]
     gen = torch.Generator(device=dev)
     gen.manual_seed(99)
@@ -351,9 +351,11 @@ def run_config3(torch, ops, harness, dev, stream, args, peaks) -> dict:
     torch.cuda.empty_cache()
     return {"value": round(gbs, 1), "unit": "GB/s",
             "pct_of_measured_hbm_peak": round(100 * gbs / peaks["hbm_gbs"], 1),
+            "traffic_bytes_per_launch": _profile_traffic("decode_kernel_config3"),
             "us_per_call": round(ms * 1e3, 2), "bytes_per_call": per_call,
             "calls": n, "context_lens": ctx.tolist(), "pool_elements_per_tensor": NB3 * BS3 * HKV3 * D3,
             "tokens_per_s": round(B3 / (ms * 1e-3), 1), "correctness_gate_max_abs": err,
+            "ctx_scale": int(args.ctx_scale),
             "kernel": "pa::decode::decode_kernel<__nv_bfloat16,128,4> (warp-specialised)"}
 
 
@@ -458,14 +460,18 @@ def run_config4(torch, ops, harness, dev, stream, args) -> dict:
     allocs = [alloc.allocate(range(S4)) for _ in range(B4)]
     ks = [torch.randn((1, H4, S4, D4), generator=gen, device=dev) for _ in range(B4)]
     vs = [torch.randn((1, H4, S4, D4), generator=gen, device=dev) for _ in range(B4)]
+    for a, kk, vv in zip(allocs, ks, vs):  # warm-up pass (also fills the pool)
+        alloc.write_kv(a.block_ids, 0, kk, vv)
     torch.cuda.synchronize()
+    reps = 5
     w0, w1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     w0.record(stream)
-    for a, kk, vv in zip(allocs, ks, vs):
-        alloc.write_kv(a.block_ids, 0, kk, vv)
+    for _ in range(reps):
+        for a, kk, vv in zip(allocs, ks, vs):
+            alloc.write_kv(a.block_ids, 0, kk, vv)
     w1.record(stream)
     torch.cuda.synchronize()
-    wkv_ms = w0.elapsed_time(w1)
+    wkv_ms = w0.elapsed_time(w1) / reps
     wkv_bytes = B4 * 2 * H4 * S4 * D4 * (4 + 2)  # fp32 read + bf16 write
     kc, vc = alloc.layer_kv(0)
     bt = alloc.block_table(allocs)
@@ -507,7 +513,8 @@ def run_config4(torch, ops, harness, dev, stream, args) -> dict:
             "kernel": "pa::prefill::prefill_tc_kernel<__nv_bfloat16,128> (tcgen05, bf16 hi/lo)",
             "write_kv": {"value": round(wkv_bytes / (wkv_ms * 1e-3) / 1e9, 1), "unit": "GB/s",
                          "bytes": wkv_bytes, "ms": round(wkv_ms, 3),
-                         "note": "4 sequences x 4096 tokens x 32 heads, fp32 device source"}}
+                         "note": "4 sequences x 4096 tokens x 32 heads, fp32 device source, "
+                                 "through TorchBlockAllocator.write_kv, mean of 5 passes after one"}}
 
 
 def _peak_tflops() -> dict:
@@ -588,6 +595,8 @@ def main() -> None:
     ap.add_argument("--no-extra", action="store_true", help="skip the config-3 GQA measurement")
     ap.add_argument("--workload", choices=["config2", "config3", "config4"], default="config2",
                     help="config3 / config4 run the GQA decode / the prefill alone (profiling)")
+    ap.add_argument("--ctx-scale", type=int, default=1,
+                    help="config3 only: multiply the seeded context lengths (fixed-cost study)")
     ap.add_argument("--pool-blocks", type=int, default=140_000,
                     help="config-3 pool blocks (140000: each K/V tensor > 2^31 elements)")
     args = ap.parse_args()

@@ -168,7 +168,7 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity,
 }
 
 // 1-D bulk async copy global -> shared (TMA engine), completing on `bar`.
-// dst, src and bytes must be multiples of 16.  Never multicast.
+// dst, src and bytes must be multiples of 16; dst is this CTA's own shared memory.
 __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes,
                                          uint64_t* bar) {
   asm volatile(

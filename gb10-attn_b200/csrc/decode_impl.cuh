@@ -14,7 +14,7 @@
 //   * One producer warp per CTA issues 1-D bulk (TMA) copies of the token
 //     rows [G kv heads x D] of K and V straight from the pages into a ring of
 //     shared-memory stages guarded by mbarriers.  A stage is 16 tokens; a row
-//     is G*D*sizeof(T) contiguous bytes of a page.  No multicast.
+//     is G*D*sizeof(T) contiguous bytes of a page, landing in this CTA only.
 //   * Each consumer warp owns one "slot": one kv head of the g-chunk and QC of
 //     the query heads that share it (GQA), so every KV byte is read from HBM
 //     once and from shared memory once per slot.  Inside a warp, R lanes

@@ -168,7 +168,7 @@ __device__ __forceinline__ void mma_commit(uint64_t* bar) {
 }
 
 // ---------------------------------------------------------------------------
-// tiled TMA load (never multicast)
+// tiled TMA load into this CTA's own shared memory
 // ---------------------------------------------------------------------------
 
 __device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, int32_t c0,

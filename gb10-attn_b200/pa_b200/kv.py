@@ -203,10 +203,12 @@ class TorchBlockAllocator:
                 t = t.pin_memory().to(self.device, non_blocking=True)
             return t
 
-        ids = torch.as_tensor(np.asarray(block_ids, dtype=np.int32)) \
-            if not isinstance(block_ids, torch.Tensor) else block_ids.to(torch.int32)
-        if ids.device.type == "cpu":
-            ids = ids.pin_memory().to(self.device, non_blocking=True)
+        # a few hundred bytes: one plain copy (pinning a fresh host buffer per
+        # call would cost far more than the copy)
+        if isinstance(block_ids, torch.Tensor):
+            ids = block_ids.to(device=self.device, dtype=torch.int32)
+        else:
+            ids = torch.as_tensor(np.asarray(block_ids, dtype=np.int32)).to(self.device)
         n_layer = self.model_cfg.n_layer
         ks = [self.pool[layer, 0] for layer in range(n_layer)]
         vs = [self.pool[layer, 1] for layer in range(n_layer)]
