@@ -68,6 +68,11 @@ struct Config {
 
 static size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
 constexpr int64_t kMaxRunCounters = int64_t(1) << 20;  // 8 MB of workspace at most
+// Extra tiles a sequence start costs in the weighted split: moving to another
+// sequence reloads the block-table window and q and publishes a piece,
+// measured at ~4-6 us on the CTAs that do it; 6 tiles measured best on the
+// config-2 shape (4 and 8 within 1 %).
+constexpr int kStartTiles = 6;
 
 // Launch epoch: tags the merge counters and the abort flag of one launch, so
 // no kernel has to zero them.  40 bits, never 0; starts from the clock so two
@@ -309,7 +314,8 @@ static int configure(const DecodeArgs& a, Config* c) {
   // Small batches: every CTA builds the plan in shared memory (no plan
   // kernel, tables beside the stage headers).
   c->fused = rows <= kFusedRows;
-  if (c->fused) c->smem += sizeof(int32_t) * (size_t)(2 * rows + 1 + 33);
+  // (scan scratch, then tile offsets, key counts, non-empty prefix)
+  if (c->fused) c->smem += kPlanScratchBytes + sizeof(int32_t) * (size_t)(3 * rows + 2);
 
   size_t off = 0;
   c->off_abort = off;
@@ -391,6 +397,7 @@ int launch(const DecodeArgs& a, void* ws, size_t ws_bytes, cudaStream_t stream) 
   p.abort_flag = reinterpret_cast<int32_t*>(w + c.off_abort);
   next_epoch(&p.epoch, &p.abort_tag);
   p.empty_fill = a.empty_fill;
+  p.beta = c.fused ? kStartTiles : 0;
   p.partials = reinterpret_cast<float*>(w + c.off_part);
   p.B = a.B * a.qlen;
   p.qlen = a.qlen;

@@ -40,6 +40,7 @@ constexpr int kTT = 16;            // tokens per pipeline stage
 constexpr int kGroup = 8;          // pieces merged per step of a split sequence
 constexpr int kFusedRows = 1024;   // rows up to which each CTA plans for itself
 constexpr int kCountBits = 24;     // arrival count bits of an epoch-tagged counter
+constexpr int kPlanScratchBytes = 272;  // scan scratch ahead of the fused plan tables
 constexpr float kNegBig = -3.0e38f;  // the reference's "minus infinity" (paged_attn_v3.cu:20)
 
 struct Params {
@@ -63,6 +64,11 @@ struct Params {
   int32_t* abort_flag;           // holds abort_tag once any pipeline wait timed out
   int32_t abort_tag;
   float empty_fill;              // rows of empty sequences (fused plan)
+  // Weighted split (fused plan only): the first tile of every sequence but
+  // the first counts as 1 + beta tiles of work, so CTAs that move on to
+  // another sequence (a block-table reload, q reload and a published piece)
+  // get fewer tiles.  0 with the plan kernel.
+  int32_t beta;
   float* partials;               // [N * 2 * NS * QC * (D + 2)]
   int64_t B, H, HKV, NB, MB, BS;
   // Query rows per block-table row: 1 for decode.  For causal prefill row
@@ -79,7 +85,7 @@ struct Params {
 
 struct __align__(16) StageHeader {
   int32_t b, gc, tok0, nvalid;
-  int32_t flags, pad0, pad1, pad2;
+  int32_t flags, seq_k, pad1, pad2;  // seq_k: ordinal among the non-empty sequences
   int64_t gt, seq_t0, seq_t1, pad3;
 };
 constexpr int kFirst = 1, kLast = 2, kEnd = 4;
@@ -128,11 +134,11 @@ static_assert(128 * 56 + 256 * 224 <= 384 * 168, "kWs8 register split exceeds la
 static_assert(128 * 40 + 512 * 104 <= 640 * 96, "kWs16 register split exceeds launch");
 
 __host__ __device__ __forceinline__ int64_t cta_lo(int64_t c, int64_t T_all, int64_t N) {
-  return T_all >= N ? c * T_all / N : (c < T_all ? c : T_all);
+  return T_all >= N ? (c * T_all + N - 1) / N : (c < T_all ? c : T_all);
 }
 // CTA whose range holds global tile t < T_all: the largest c with cta_lo(c) <= t.
 __host__ __device__ __forceinline__ int64_t cta_of(int64_t t, int64_t T_all, int64_t N) {
-  return T_all >= N ? ((t + 1) * N - 1) / T_all : t;
+  return T_all >= N ? t * N / T_all : t;
 }
 
 // One arrival on an epoch-tagged counter (value = epoch << kCountBits |
@@ -151,15 +157,18 @@ __device__ __forceinline__ int epoch_arrive(unsigned long long* counter, unsigne
 }
 
 // The plan of one launch built by every CTA in shared memory (B <= kFusedRows
-// rows; scratch = 33 words): tile_off_s[b] = tiles of rows 0..b-1, ntok_s[b] = keys row b reads
+// rows; scratch = 33 64-bit words): ne_s[b] = non-empty rows before b;
+// tile_off_s[b] = tiles of rows 0..b-1, ntok_s[b] = keys row b reads
 // (the plan kernel's rule: a query row s of qlen sees context - qlen + s + 1
 // keys, clamped to the block table).  CTA b % gridDim fills the output rows of
 // empty sequences (the reference's v3 yields NaN there, paged_attn_v3.cu:160-165).
 template <int D>
 __device__ __forceinline__ void fused_plan(const Params& p, int32_t* tile_off_s, int32_t* ntok_s,
-                                           int32_t* scratch) {
-  int32_t* warp_tot = scratch;     // [32]
-  int32_t& carry_s = scratch[32];
+                                           int32_t* ne_s, long long* scratch) {
+  // one scan carries both counts: tiles in the high bits, non-empty rows in
+  // the low 16 (rows <= kFusedRows < 2^16)
+  long long* warp_tot = scratch;     // [32]
+  long long& carry_s = scratch[32];
   const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5, nw = blockDim.x >> 5;
   const int64_t max_ctx = p.MB * p.BS;
   if (tid == 0) carry_s = 0;
@@ -184,31 +193,39 @@ __device__ __forceinline__ void fused_plan(const Params& p, int32_t* tile_off_s,
       ntok_s[b] = (int32_t)n;
       tiles = (int32_t)((n + kTT - 1) / kTT);
     }
-    int32_t x = tiles;
+    const long long mine = ((long long)tiles << 16) | (tiles > 0 ? 1 : 0);
+    long long x = mine;
 #pragma unroll
     for (int o = 1; o < 32; o <<= 1) {
-      const int32_t y = __shfl_up_sync(0xffffffffu, x, o);
+      const long long y = __shfl_up_sync(0xffffffffu, x, o);
       if (lane >= o) x += y;
     }
     if (lane == 31) warp_tot[wid] = x;
     __syncthreads();
     if (wid == 0) {
-      int32_t w = lane < nw ? warp_tot[lane] : 0;
+      long long w = lane < nw ? warp_tot[lane] : 0;
 #pragma unroll
       for (int o = 1; o < 32; o <<= 1) {
-        const int32_t y = __shfl_up_sync(0xffffffffu, w, o);
+        const long long y = __shfl_up_sync(0xffffffffu, w, o);
         if (lane >= o) w += y;
       }
       if (lane < nw) warp_tot[lane] = w;  // inclusive over warps
     }
     __syncthreads();
-    const int32_t carry = carry_s;
-    if (b < p.B) tile_off_s[b] = carry + (wid ? warp_tot[wid - 1] : 0) + x - tiles;
+    const long long carry = carry_s;
+    if (b < p.B) {
+      const long long excl = carry + (wid ? warp_tot[wid - 1] : 0) + x - mine;
+      tile_off_s[b] = (int32_t)(excl >> 16);
+      ne_s[b] = (int32_t)(excl & 0xffff);
+    }
     __syncthreads();
     if (tid == 0) carry_s = carry + warp_tot[nw - 1];
     __syncthreads();
   }
-  if (tid == 0) tile_off_s[p.B] = carry_s;
+  if (tid == 0) {
+    tile_off_s[p.B] = (int32_t)(carry_s >> 16);
+    ne_s[p.B] = (int32_t)(carry_s & 0xffff);
+  }
   __syncthreads();
 }
 
@@ -304,18 +321,35 @@ __global__ void __launch_bounds__(Limits<T, D, QC>::THREADS, 1)
   // global round trips when the producer moves to the next sequence.
   const int32_t* tile_off = p.tile_off;
   const int32_t* ntok_s = nullptr;
+  const int32_t* ne_s = nullptr;
   if (tile_off == nullptr) {
-    int32_t* to_s = reinterpret_cast<int32_t*>(hdr + nstage);
+    unsigned char* plan_base = reinterpret_cast<unsigned char*>(hdr + nstage);
+    int32_t* to_s = reinterpret_cast<int32_t*>(plan_base + kPlanScratchBytes);
     int32_t* nt_s = to_s + p.B + 1;
-    fused_plan<D>(p, to_s, nt_s, nt_s + p.B);
+    int32_t* nz_s = nt_s + p.B;
+    fused_plan<D>(p, to_s, nt_s, nz_s, reinterpret_cast<long long*>(plan_base));
     tile_off = to_s;
     ntok_s = nt_s;
+    ne_s = nz_s;
   }
 
   const int64_t Tpg = tile_off[p.B];  // tiles per g-chunk
   const int64_t T_all = Tpg * p.NGC;
   const int64_t cta = blockIdx.x;
-  const int64_t lo = cta_lo(cta, T_all, p.N), hi = cta_lo(cta + 1, T_all, p.N);
+  // Weighted stream-K split.  Tile t of the k-th non-empty sequence costs
+  // from t + beta * k on, C is the total; CTA c owns the tiles whose cost
+  // lies in [ceil(c C / N), ceil((c+1) C / N)).  beta is used only while
+  // every CTA's share (>= 2 beta + 2) outweighs the jump at a sequence start,
+  // so no CTA is left without tiles.
+  const int64_t Kseq = ne_s ? (int64_t)p.NGC * ne_s[p.B] : 0;
+  const int64_t beta = (ne_s && p.beta > 0 && T_all >= p.N &&
+                        T_all + (int64_t)p.beta * (Kseq - 1) >= (int64_t)p.N * (2 * p.beta + 2))
+                           ? p.beta : 0;
+  const int64_t Ccost = T_all + beta * (Kseq > 0 ? Kseq - 1 : 0);
+  // CTA owning tile t of the sequence with ordinal k
+  auto owner = [&](int64_t t, int64_t k) -> int64_t {
+    return T_all >= p.N ? (t + beta * k) * p.N / Ccost : t;
+  };
 
   if constexpr (WS) {
     if (warp < 4) {
@@ -330,6 +364,42 @@ __global__ void __launch_bounds__(Limits<T, D, QC>::THREADS, 1)
 
   if (is_producer) {
     // ------------------------------------------------------------------ producer
+    // This CTA's tiles [lo, hi).  Weighted split: the first non-empty
+    // sequence whose last tile's cost reaches each bound, found by the 32
+    // lanes over 32 sequences at a time.
+    int64_t lo, hi, lo_seq = -1;
+    if (beta == 0) {
+      lo = cta_lo(cta, T_all, p.N);
+      hi = cta_lo(cta + 1, T_all, p.N);
+    } else {
+      const int64_t t_lo = (cta * Ccost + p.N - 1) / p.N;
+      const int64_t t_hi = cta + 1 >= p.N ? Ccost : ((cta + 1) * Ccost + p.N - 1) / p.N;
+      const int Bi = (int)p.B, S = p.NGC * Bi, Kr = ne_s[p.B];
+      int s_lo = -1, s_hi = -1;
+      for (int base = 0; base < S && (s_lo < 0 || s_hi < 0); base += 32) {
+        const int sq = base + lane;
+        long long cl = -1;  // empty rows never qualify
+        if (sq < S) {
+          const int g = sq / Bi, bb = sq - g * Bi;
+          if (tile_off[bb + 1] > tile_off[bb])
+            cl = (long long)g * Tpg + tile_off[bb + 1] - 1 + beta * ((long long)g * Kr + ne_s[bb]);
+        }
+        const unsigned m_lo = __ballot_sync(0xffffffffu, cl >= t_lo);
+        const unsigned m_hi = __ballot_sync(0xffffffffu, cl >= t_hi);
+        if (s_lo < 0 && m_lo) s_lo = base + __ffs(m_lo) - 1;
+        if (s_hi < 0 && m_hi) s_hi = base + __ffs(m_hi) - 1;
+      }
+      // first tile whose cost reaches t: within sequence sq, or its first tile
+      auto tile_at = [&](int sq, int64_t t) -> int64_t {
+        const int g = sq / Bi, bb = sq - g * Bi;
+        const int64_t start = (int64_t)g * Tpg + tile_off[bb];
+        const int64_t x = t - beta * ((int64_t)g * Kr + ne_s[bb]);
+        return x > start ? x : start;
+      };
+      lo = s_lo >= 0 ? tile_at(s_lo, t_lo) : T_all;
+      hi = (cta + 1 >= p.N || s_hi < 0) ? T_all : tile_at(s_hi, t_hi);
+      lo_seq = s_lo;
+    }
     int stage = 0;
     uint32_t phase = 0;
     bool ok = true;
@@ -338,7 +408,9 @@ __global__ void __launch_bounds__(Limits<T, D, QC>::THREADS, 1)
       int gc = (int)(lo / Tpg);
       int64_t r = lo - (int64_t)gc * Tpg;
       int b;
-      if (p.cta_seq) {
+      if (lo_seq >= 0) {  // weighted split: the search found it
+        b = (int)(lo_seq % p.B);
+      } else if (p.cta_seq) {
         b = p.cta_seq[cta];
       } else {  // upper_bound(tile_off[0..B], r) - 1
         int64_t a = 0, z = p.B + 1;
@@ -359,6 +431,12 @@ __global__ void __launch_bounds__(Limits<T, D, QC>::THREADS, 1)
         return n < 0 ? 0 : n;
       };
       int64_t n_tok = seq_len(b);
+      // ordinal of the sequence among the non-empty ones (the weighted
+      // split's cost of its tiles; carried to the consumers' merges)
+      auto ordinal = [&](int g, int bb) -> int32_t {
+        return ne_s ? (int32_t)((int64_t)g * ne_s[p.B] + ne_s[bb]) : 0;
+      };
+      int32_t seq_k = ordinal(gc, b);
       const int32_t* bt = p.block_tables + (int64_t)(b / p.qlen) * p.MB;
       auto bt_load = [&](int64_t idx) -> int32_t {
         return (idx >= 0 && idx < p.MB) ? __ldg(bt + idx) : 0;
@@ -408,6 +486,7 @@ __global__ void __launch_bounds__(Limits<T, D, QC>::THREADS, 1)
           h.tok0 = (int32_t)tok0;
           h.nvalid = nvalid;
           h.flags = (first ? kFirst : 0) | ((gt + 1 == hi || r + 1 == s1) ? kLast : 0);
+          h.seq_k = seq_k;
           h.gt = gt;
           h.seq_t0 = (int64_t)gc * Tpg + s0;
           h.seq_t1 = (int64_t)gc * Tpg + s1;
@@ -461,6 +540,7 @@ __global__ void __launch_bounds__(Limits<T, D, QC>::THREADS, 1)
           s0 = tile_off[b];
           s1 = tile_off[b + 1];
           n_tok = seq_len(b);
+          seq_k = ordinal(gc, b);
           bt = p.block_tables + (int64_t)(b / p.qlen) * p.MB;
           win_base = 0;  // the new sequence starts at its first page
           win_cur = nx_cur;
@@ -507,13 +587,14 @@ __global__ void __launch_bounds__(Limits<T, D, QC>::THREADS, 1)
   // each run of kGroup consecutive pieces folds them into the run's first
   // slot, and the last run to finish merges the run results.
   const int64_t pstride = (int64_t)QC * (D + 2);
-  auto publish = [&](int pb, int pgc, int64_t phead0, int64_t t0, int64_t t1) {
-    const int64_t first = cta_of(t0, T_all, p.N);
-    const int64_t last = cta_of(t1 - 1, T_all, p.N);
+  auto publish = [&](int pb, int pgc, int64_t phead0, int64_t t0, int64_t t1, int64_t k) {
+    const int64_t first = owner(t0, k);
+    const int64_t last = owner(t1 - 1, k);
     const int64_t npieces = last - first + 1;
     // A CTA's first segment sits in partial slot 0, a later one in slot 1:
     // only the first CTA of a sequence can hold it as a later segment.
-    const bool first_late = cta_lo(first, T_all, p.N) < t0;
+    // (tile t0 - 1 is the last tile of the previous non-empty sequence)
+    const bool first_late = t0 > 0 && owner(t0 - 1, k - 1) == first;
     auto piece = [&](int64_t c) -> float* {
       const int o2 = (c == first && first_late) ? 1 : 0;
       return p.partials + ((c * 2 + o2) * NS + slot) * pstride;
@@ -771,7 +852,7 @@ __global__ void __launch_bounds__(Limits<T, D, QC>::THREADS, 1)
           }
         }
       }
-      publish(b, gc, head0, h.seq_t0, h.seq_t1);
+      publish(b, gc, head0, h.seq_t0, h.seq_t1, h.seq_k);
     }
     ++seg_count;
   }

@@ -124,6 +124,26 @@ def test_long_sequences_two_level_merge(num_splits):
             assert abs(lse[b, h] - want) < 1e-3
 
 
+def test_weighted_split_ragged_batch():
+    """Enough tiles over the automatic split (148 CTAs on a B200) that the
+    split weights each sequence start as extra tiles: ragged lengths, an
+    empty sequence and a one-token one; out and lse against the oracle."""
+    ctxs = [9000, 0, 7000, 1, 8500, 9000, 40]
+    q, k, v, bt, ctx = case(17, len(ctxs), 8, 2, 64, 16, ctxs, "float16")
+    scale = 0.125
+    out, lse = abi_decode(q, k, v, bt, ctx, scale, "float16", want_lse=True)
+    want = orc.decode(q, k, v, bt, ctx, scale)
+    live = [b for b, c in enumerate(ctxs) if c > 0]
+    assert max_abs(out[live], want[live]) <= 2e-3
+    assert np.isnan(out[1]).all()  # empty sequence: NaN row, as the v3 entry point
+    for b in (0, 3, 6):
+        n = int(ctx[b])
+        ks = k[bt[b, :(n + 15) // 16]].reshape(-1, 2, 64)[:n].astype(np.float64)
+        for h in (0, 7):
+            s_ = scale * ks[:, h // 4] @ q[b, h].astype(np.float64)
+            assert abs(lse[b, h] - (s_.max() + np.log(np.exp(s_ - s_.max()).sum()))) < 1e-3
+
+
 def test_hip_selftest_fixture():
     """The reference's own HIP self-test (mt19937(7) inputs, tolerance 3e-4,
     rocm/hip/paged_attn_v1_hip.cpp:151-198) run on the B200 kernel."""
