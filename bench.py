@@ -378,20 +378,45 @@ def correctness_gate(torch, layer_call, pool, q, bt_np, bt_dev, ctx_dev, scale, 
 
 def run_e2e(torch, dist, args, layer_call, q_dev, tables, ctx_np, dev, stream, world, L,
             REGIONS):
-    """Same decode steps through the public API with host buffers: q and the
-    block table copied host->device and the outputs device->host each step."""
+    """Same decode steps through the public API with host buffers, as a serving
+    loop runs them: every step copies its q (all layers) and block table from
+    pinned host memory to the device and reads every layer's output back to
+    pinned host memory, all inside the timed region.  The copies go on a side
+    stream: layer l+1's q slice travels while layer l computes, and layer l's
+    output is read back while layer l+1 computes; the step's block table and
+    context lengths, and layer 0's q, are copied before its first kernel."""
     q_host = torch.empty(tuple(q_dev.shape), dtype=torch.float32).pin_memory()
     q_host.copy_(q_dev.cpu())
     bt_host = [torch.from_numpy(t).pin_memory() for t in tables]
     ctx_host = torch.from_numpy(ctx_np).pin_memory()
     out_host = torch.empty(tuple(q_dev.shape), dtype=torch.float32).pin_memory()
+    qd = torch.empty_like(q_dev)
+    btd = torch.empty(tuple(tables[0].shape), dtype=torch.int32, device=dev)
+    cd = torch.empty(len(ctx_np), dtype=torch.int32, device=dev)
+    copy = torch.cuda.Stream(device=dev)
+    ev_in = [torch.cuda.Event() for _ in range(L)]
+    ev_out = [torch.cuda.Event() for _ in range(L)]
 
     def e2e_step(i: int):
-        qd = q_host.to(dev, non_blocking=True)
-        btd = bt_host[i % REGIONS].to(dev, non_blocking=True)
-        cd = ctx_host.to(dev, non_blocking=True)
+        # inputs of this step: the device buffers are free once the previous
+        # step's last output was read back (the copy stream is in order)
+        with torch.cuda.stream(copy):
+            btd.copy_(bt_host[i % REGIONS], non_blocking=True)
+            cd.copy_(ctx_host, non_blocking=True)
+            qd[0].copy_(q_host[0], non_blocking=True)
+            ev_in[0].record(copy)
         for layer in range(L):
-            out_host[layer].copy_(layer_call(layer, qd[layer], btd, cd), non_blocking=True)
+            if layer + 1 < L:
+                with torch.cuda.stream(copy):
+                    qd[layer + 1].copy_(q_host[layer + 1], non_blocking=True)
+                    ev_in[layer + 1].record(copy)
+            stream.wait_event(ev_in[layer])
+            out = layer_call(layer, qd[layer], btd, cd)
+            ev_out[layer].record(stream)
+            with torch.cuda.stream(copy):
+                copy.wait_event(ev_out[layer])
+                out_host[layer].copy_(out, non_blocking=True)
+                out.record_stream(copy)
 
     for i in range(max(2, args.warmup)):
         e2e_step(i)
@@ -399,11 +424,19 @@ def run_e2e(torch, dist, args, layer_call, q_dev, tables, ctx_np, dev, stream, w
     if world > 1:
         dist.barrier()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    done = torch.cuda.Event()
     e0.record(stream)
+    copy.wait_event(e0)  # no copy of the timed steps starts before e0
     for i in range(args.steps):
         e2e_step(i)
+    done.record(copy)
+    stream.wait_event(done)  # the last read-back is inside the timed region
     e1.record(stream)
     torch.cuda.synchronize()
+    # the overlapped loop must read back what a plain call computes
+    want = layer_call(L - 1, qd[L - 1], btd, cd).cpu()
+    if not torch.equal(out_host[L - 1], want):
+        raise SystemExit("e2e read-back differs from a direct call")
     h2d = q_host.numel() * 4 + bt_host[0].numel() * 4 + ctx_host.numel() * 4
     d2h = out_host.numel() * 4
     return e0.elapsed_time(e1), h2d, d2h
