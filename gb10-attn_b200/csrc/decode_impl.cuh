@@ -88,7 +88,7 @@ struct __align__(16) StageHeader {
   int32_t flags, seq_k, pad1, pad2;  // seq_k: ordinal among the non-empty sequences
   int64_t gt, seq_t0, seq_t1, pad3;
 };
-constexpr int kFirst = 1, kLast = 2, kEnd = 4;
+constexpr int kFirst = 1, kLast = 2, kEnd = 4, kCtaLast = 8;
 
 // Lane geometry for element type T and head_dim D.
 template <typename T, int D>
@@ -281,6 +281,57 @@ __device__ __forceinline__ void merge_pieces(PtrFn ptr, int64_t c0, int64_t stri
   for (int j = 0; j < QC; ++j)
 #pragma unroll
     for (int off = 16; off >= 1; off >>= 1) lg[j] += __shfl_xor_sync(0xffffffffu, lg[j], off);
+}
+
+// The same merge with every lane reading whole states, U at a time: the
+// maxima, sums and O elements of U states are all in flight together and are
+// folded in with the online log-sum-exp rule.  Needs ~24 registers per state
+// per lane, so it runs where the consumer's q and accumulator registers are
+// no longer live.
+template <int QC, int D, int U, typename PtrFn>
+__device__ __forceinline__ void merge_pieces_wide(PtrFn ptr, int64_t c0, int64_t stride,
+                                                  int64_t count, int lane, float (&o)[QC * D / 32],
+                                                  float (&mg)[QC], float (&lg)[QC]) {
+  constexpr int PER = QC * D / 32;
+#pragma unroll
+  for (int j = 0; j < QC; ++j) { mg[j] = kNegBig; lg[j] = 0.f; }
+#pragma unroll
+  for (int k = 0; k < PER; ++k) o[k] = 0.f;
+  for (int64_t k0 = 0; k0 < count; k0 += U) {
+    float ms[U][QC], ls[U][QC], os[U][PER];
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      if (k0 + u < count) {
+        const float* pc = ptr(c0 + (k0 + u) * stride);
+#pragma unroll
+        for (int j = 0; j < QC; ++j) {
+          ms[u][j] = __ldcg(pc + QC * D + j);
+          ls[u][j] = __ldcg(pc + QC * D + QC + j);
+        }
+#pragma unroll
+        for (int q = 0; q < PER; ++q) os[u][q] = __ldcg(pc + lane + 32 * q);
+      } else {
+#pragma unroll
+        for (int j = 0; j < QC; ++j) { ms[u][j] = kNegBig; ls[u][j] = 0.f; }
+#pragma unroll
+        for (int q = 0; q < PER; ++q) os[u][q] = 0.f;
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      float a[QC], b[QC];
+#pragma unroll
+      for (int j = 0; j < QC; ++j) {
+        const float mn = fmaxf(mg[j], ms[u][j]);
+        a[j] = fast_exp2(mg[j] - mn);
+        b[j] = fast_exp2(ms[u][j] - mn);
+        lg[j] = lg[j] * a[j] + ls[u][j] * b[j];
+        mg[j] = mn;
+      }
+#pragma unroll
+      for (int q = 0; q < PER; ++q) o[q] = o[q] * a[(32 * q) / D] + os[u][q] * b[(32 * q) / D];
+    }
+  }
 }
 
 template <typename T, int D, int QC>
@@ -485,7 +536,8 @@ __global__ void __launch_bounds__(Limits<T, D, QC>::THREADS, 1)
           h.gc = gc;
           h.tok0 = (int32_t)tok0;
           h.nvalid = nvalid;
-          h.flags = (first ? kFirst : 0) | ((gt + 1 == hi || r + 1 == s1) ? kLast : 0);
+          h.flags = (first ? kFirst : 0) | ((gt + 1 == hi || r + 1 == s1) ? kLast : 0) |
+                    (gt + 1 == hi ? kCtaLast : 0);
           h.seq_k = seq_k;
           h.gt = gt;
           h.seq_t0 = (int64_t)gc * Tpg + s0;
@@ -587,7 +639,9 @@ __global__ void __launch_bounds__(Limits<T, D, QC>::THREADS, 1)
   // each run of kGroup consecutive pieces folds them into the run's first
   // slot, and the last run to finish merges the run results.
   const int64_t pstride = (int64_t)QC * (D + 2);
-  auto publish = [&](int pb, int pgc, int64_t phead0, int64_t t0, int64_t t1, int64_t k) {
+  // `wide`: called after the consumer loop, where the wide merge fits in the
+  // registers (inside the loop the q and accumulator state is live).
+  auto publish = [&](int pb, int pgc, int64_t phead0, int64_t t0, int64_t t1, int64_t k, bool wide) {
     const int64_t first = owner(t0, k);
     const int64_t last = owner(t1 - 1, k);
     const int64_t npieces = last - first + 1;
@@ -617,7 +671,8 @@ __global__ void __launch_bounds__(Limits<T, D, QC>::THREADS, 1)
       go = arrive(&p.grp_counters[(g0 * 2 + o2) * NS + slot]) == (int)(g1 - g0);
       if (go) {
         __threadfence();
-        merge_pieces<QC, D>(piece, g0, 1, g1 - g0 + 1, lane, o, mg, lg);
+        if (wide) merge_pieces_wide<QC, D, 4>(piece, g0, 1, g1 - g0 + 1, lane, o, mg, lg);
+        else merge_pieces<QC, D>(piece, g0, 1, g1 - g0 + 1, lane, o, mg, lg);
         float* dst = piece(g0);  // read above; now holds the run's merged state
 #pragma unroll
         for (int k = 0; k < PER; ++k) dst[lane + 32 * k] = o[k];
@@ -633,7 +688,8 @@ __global__ void __launch_bounds__(Limits<T, D, QC>::THREADS, 1)
     }
     if (go && arrive(&p.counters[((int64_t)pgc * p.B + pb) * NS + slot]) == (int)(n_top - 1)) {
       __threadfence();
-      merge_pieces<QC, D>(piece, first, top_stride, n_top, lane, o, mg, lg);
+      if (wide) merge_pieces_wide<QC, D, 4>(piece, first, top_stride, n_top, lane, o, mg, lg);
+      else merge_pieces<QC, D>(piece, first, top_stride, n_top, lane, o, mg, lg);
 #pragma unroll
       for (int k = 0; k < PER; ++k) {
         const int j = (32 * k) / D;
@@ -648,6 +704,10 @@ __global__ void __launch_bounds__(Limits<T, D, QC>::THREADS, 1)
     }
   };
 
+  bool pend = false;  // the CTA's final split piece, published after the loop
+  int pend_b = 0, pend_gc = 0;
+  int64_t pend_head0 = 0, pend_t0 = 0, pend_t1 = 0, pend_k = 0;
+
   int stage = 0;
   uint32_t phase = 0;
   int seg_count = 0;
@@ -661,7 +721,10 @@ __global__ void __launch_bounds__(Limits<T, D, QC>::THREADS, 1)
       break;
     }
     const StageHeader h = hdr[stage];
-    if (h.flags & kEnd) break;
+    if (h.flags & kEnd) {
+      if (pend) publish(pend_b, pend_gc, pend_head0, pend_t0, pend_t1, pend_k, true);
+      break;
+    }
 
     if (h.flags & kFirst) {
       b = h.b;
@@ -852,7 +915,19 @@ __global__ void __launch_bounds__(Limits<T, D, QC>::THREADS, 1)
           }
         }
       }
-      publish(b, gc, head0, h.seq_t0, h.seq_t1, h.seq_k);
+      // The CTA's final segment is published once the loop is left (the
+      // next stage is the end marker), with the wide merge.
+      if (h.flags & kCtaLast) {
+        pend = true;
+        pend_b = b;
+        pend_gc = gc;
+        pend_head0 = head0;
+        pend_t0 = h.seq_t0;
+        pend_t1 = h.seq_t1;
+        pend_k = h.seq_k;
+      } else {
+        publish(b, gc, head0, h.seq_t0, h.seq_t1, h.seq_k, false);
+      }
     }
     ++seg_count;
   }
