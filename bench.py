@@ -174,7 +174,9 @@ def run_b200(args) -> None:
     bt_dev = [torch.from_numpy(t).to(dev) for t in tables]
     ctx_dev = torch.from_numpy(ctx_np).to(dev)
     scale = D ** -0.5
-    outs = torch.empty((L, B, H, D), dtype=torch.float32, device=dev)
+    # each call returns its own output tensor; keeping references (not copying
+    # into one buffer) leaves nothing but decode kernels on the stream
+    outs = [None] * L
     stream = torch.cuda.current_stream()
 
     bytes_per_call = harness.decode_bytes(ctx_np, H, HKV, D, 2, BS)
@@ -396,8 +398,14 @@ def run_e2e(torch, dist, args, layer_call, q_dev, tables, ctx_np, dev, stream, w
     copy = torch.cuda.Stream(device=dev)
     ev_in = [torch.cuda.Event() for _ in range(L)]
     ev_out = [torch.cuda.Event() for _ in range(L)]
+    d2h_done = torch.cuda.Event()
+    held = []  # this step's outputs, alive until their read-back is done
 
     def e2e_step(i: int):
+        # the previous step's outputs are released once the compute stream has
+        # waited for their read-back (stream-ordered reuse, no allocator sync)
+        stream.wait_event(d2h_done)
+        held.clear()
         # inputs of this step: the device buffers are free once the previous
         # step's last output was read back (the copy stream is in order)
         with torch.cuda.stream(copy):
@@ -412,11 +420,12 @@ def run_e2e(torch, dist, args, layer_call, q_dev, tables, ctx_np, dev, stream, w
                     ev_in[layer + 1].record(copy)
             stream.wait_event(ev_in[layer])
             out = layer_call(layer, qd[layer], btd, cd)
+            held.append(out)
             ev_out[layer].record(stream)
             with torch.cuda.stream(copy):
                 copy.wait_event(ev_out[layer])
                 out_host[layer].copy_(out, non_blocking=True)
-                out.record_stream(copy)
+        d2h_done.record(copy)
 
     for i in range(max(2, args.warmup)):
         e2e_step(i)
