@@ -8,9 +8,12 @@
 //
 //   * Work unit = a tile of kTT = 16 consecutive tokens of one sequence for a
 //     group of G kv heads ("g-chunk").  The NGC * sum_b ceil(ctx_b / 16) tiles
-//     are split into N equal contiguous ranges, one per CTA (N = SMs x
-//     resident CTAs for automatic splitting), so every SM streams the same
-//     number of bytes whatever the context lengths (stream-K style).
+//     are split into N contiguous ranges, one per CTA (N = SMs x resident CTAs
+//     for automatic splitting), so every SM streams about the same number of
+//     bytes whatever the context lengths (stream-K style).  The ranges are
+//     equal in cost: a sequence start counts as extra tiles (Params::beta).
+//     For batches up to kFusedRows rows every CTA builds the plan (tile
+//     offsets) in shared memory itself; larger ones use the plan kernel.
 //   * One producer warp per CTA issues 1-D bulk (TMA) copies of the token
 //     rows [G kv heads x D] of K and V straight from the pages into a ring of
 //     shared-memory stages guarded by mbarriers.  A stage is 16 tokens; a row
@@ -23,8 +26,9 @@
 //     softmax state (m, l, acc) in registers; the row groups are merged with
 //     shuffles once per segment, not per token.
 //   * A sequence whose tiles span several CTAs is merged by the CTA that
-//     finishes its piece last (per-(sequence, slot) arrival counter), so no
-//     second kernel and no extra partial round trip for unsplit sequences.
+//     finishes its piece last (per-(sequence, slot) arrival counter, two
+//     levels for long sequences), so no second kernel and no extra partial
+//     round trip for unsplit sequences.
 //
 // Scores are kept in the log2 domain (q pre-scaled by scale*log2(e)) so each
 // exponential is one ex2.approx; the reference's __expf is the same
