@@ -21,6 +21,10 @@ N > 1      one process per GPU (torchrun); each rank runs the same per-GPU
            workload (weak scaling, batch sharding: no collective on the data
            path); value = all ranks' bytes / slowest rank's time.
 
+--workload config5 (torchrun) prints the multi-GPU
+lines: the batch shard at 64 sequences x ctx 8192 per GPU, and one 1,048,576-
+token GQA sequence split over the ranks with its partials merged over NVLink.
+
 --impl reference times the reference's scalar FP32 CPU decode (the oracle's
 restatement of gb10-attn rocm/hip/paged_attn_v1_hip.cpp:104-141; the HIP file
 itself does not build here) on the host cores, on a bounded sample of the
@@ -594,6 +598,164 @@ def run_config3_only(args) -> None:
                       "workload": "configs[2]", "detail": r}), flush=True)
 
 
+def run_config5(args) -> None:
+    """BASELINE.json configs[4], one process per GPU (torchrun).  (A) batch
+    shard: gpt2 fp16 decode, 64 sequences of ctx 8192 per GPU, `--layers`
+    layer pools with 2 cold regions, no collective; (B) one sequence of
+    1,048,576 tokens, 32 query / 8 KV heads, D=128, bf16, its token range split
+    evenly over the ranks: each decodes its range (paged_attention_v3_lse),
+    the (out, lse) partials cross NVLink in one all-gather and are merged
+    (pa_b200.dist.sequence_sharded_decode).  Times are the max over ranks;
+    the B output is checked against per-rank dense fp32 partials merged with
+    the same rule."""
+    import datetime
+
+    import torch
+    import torch.distributed as dist
+
+    from pa_b200 import dist as padist
+    from pa_b200 import harness, ops
+
+    rank, local, world = _env_rank()
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+    peaks = _peaks()
+    stream = torch.cuda.current_stream()
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(5000 + rank)
+
+    def max_over_ranks(ms: float) -> float:
+        t = torch.tensor([ms], dtype=torch.float64, device=dev)
+        if world > 1:
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    def timed(fn, n: int) -> float:
+        for i in range(args.warmup):
+            fn(i)
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for i in range(n):
+            fn(i)
+        e1.record(stream)
+        torch.cuda.synchronize()
+        return max_over_ranks(e0.elapsed_time(e1))
+
+    # (A) batch shard ------------------------------------------------------
+    BA, CTXA, RA, LA = 64, 8192, 2, args.layers
+    nb = BA * (CTXA // BS) * RA
+    pools = []
+    for _ in range(LA):
+        t = torch.empty((2, nb, BS, HKV, D), dtype=torch.float16, device=dev)
+        t.normal_(generator=gen)
+        pools.append(t)
+    qa = torch.randn((LA, BA, H, D), generator=gen, device=dev)
+    ctxa = np.full(BA, CTXA, np.int32)
+    bta = [torch.from_numpy(t).to(dev) for t in harness.cold_regions([CTXA // BS] * BA, RA, nb,
+                                                                        seed=rank)]
+    ctxa_d = torch.from_numpy(ctxa).to(dev)
+    outs = [None] * LA
+
+    def step_a(i: int):
+        for layer in range(LA):
+            outs[layer] = ops.paged_attention_v3(qa[layer], pools[layer][0], pools[layer][1],
+                                                 bta[i % RA], ctxa_d, D ** -0.5, 0)
+
+    ms_a = timed(step_a, args.steps)
+    bytes_a = LA * harness.decode_bytes(ctxa, H, HKV, D, 2, BS) * world * args.steps
+    gbs_a = bytes_a / (ms_a * 1e-3) / 1e9
+    del pools, outs, qa
+    torch.cuda.empty_cache()
+
+    # (B) one long sequence over the ranks ----------------------------------
+    NT, H5, HKV5, D5, R5 = 1 << 20, 32, 8, 128, 2
+    nt = NT // world  # this rank's token range [rank * nt, (rank + 1) * nt)
+    need = nt // BS
+    kv = torch.empty((2, R5 * need, BS, HKV5, D5), dtype=torch.bfloat16, device=dev)
+    kv.normal_(generator=gen)
+    perm = np.random.default_rng(77 + rank).permutation(R5 * need).astype(np.int32)
+    btb = [torch.from_numpy(perm[r * need:(r + 1) * need].reshape(1, need).copy()).to(dev)
+           for r in range(R5)]
+    ctxb = torch.tensor([nt], dtype=torch.int32, device=dev)
+    qgen = torch.Generator(device=dev)
+    qgen.manual_seed(55)  # the same q on every rank
+    qb = torch.randn((1, H5, D5), generator=qgen, device=dev)
+    scale5 = D5 ** -0.5
+    group = dist.group.WORLD if world > 1 else None
+
+    def decode_b(i: int):
+        if world == 1:
+            return ops.paged_attention_v3(qb, kv[0], kv[1], btb[i % R5], ctxb, scale5, 0)
+        return padist.sequence_sharded_decode(qb, kv[0], kv[1], btb[i % R5], ctxb, scale5, group)
+
+    # gate: dense fp32 partial of this rank's range, merged over the ranks
+    got = decode_b(0)
+    blocks = btb[0][0].long()
+    kk = kv[0][blocks].float().reshape(nt, HKV5, D5).repeat_interleave(H5 // HKV5, dim=1)
+    sc = torch.einsum("hd,thd->ht", qb[0], kk) * scale5
+    del kk
+    m = sc.max(dim=1).values
+    p_ = torch.exp(sc - m[:, None])
+    del sc
+    vv = kv[1][blocks].float().reshape(nt, HKV5, D5).repeat_interleave(H5 // HKV5, dim=1)
+    o_loc = torch.einsum("ht,thd->hd", p_, vv) / p_.sum(1)[:, None]
+    lse_loc = m + torch.log(p_.sum(1))
+    del vv, p_
+    if world > 1:
+        outs_all = [torch.empty_like(o_loc) for _ in range(world)]
+        lses_all = [torch.empty_like(lse_loc) for _ in range(world)]
+        dist.all_gather(outs_all, o_loc)
+        dist.all_gather(lses_all, lse_loc)
+        ls = torch.stack(lses_all)
+        w = torch.exp(ls - ls.max(0).values)
+        want = (torch.stack(outs_all) * w[..., None]).sum(0) / w.sum(0)[:, None]
+    else:
+        want = o_loc
+    err_b = float((got[0] - want).abs().max())
+    err_b = max_over_ranks(err_b)
+    torch.cuda.empty_cache()
+
+    ms_b = timed(decode_b, args.steps)
+    # the same decode without the exchange: how much the all-gather + merge add
+    ms_b_local = timed(lambda i: ops.paged_attention_v3_lse(qb, kv[0], kv[1], btb[i % R5], ctxb,
+                                                            scale5, 0), args.steps)
+    bytes_b = NT * HKV5 * D5 * 2 * 2 * args.steps
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank == 0:
+        line = {
+            "metric": METRIC, "workload": "configs[4]", "n_gpus": world,
+            "value": round(gbs_a, 1), "unit": "GB/s", "steps": args.steps,
+            "warmup": args.warmup, "scaling": "weak", "higher_is_better": True,
+            "data": "synthetic N(0,1) KV pools and q, seeded",
+            "batch_shard": {
+                "value": round(gbs_a, 1), "unit": "GB/s",
+                "pct_of_measured_hbm_peak": round(100 * gbs_a / world / peaks["hbm_gbs"], 1),
+                "config": f"gpt2 fp16, {BA} sequences x ctx {CTXA} per GPU, {LA} layers, "
+                          f"{RA} cold regions; no collective",
+                "ms_per_step": round(ms_a / args.steps, 4),
+                "tokens_per_s": round(BA * world * args.steps / (ms_a * 1e-3), 1)},
+            "sequence_sharded": {
+                "value": round(bytes_b / (ms_b * 1e-3) / 1e9, 1), "unit": "GB/s",
+                "pct_of_measured_hbm_peak": round(100 * bytes_b / (ms_b * 1e-3) / 1e9 / world
+                                                  / peaks["hbm_gbs"], 1),
+                "config": f"1 sequence of {NT} tokens, 32q/8kv, D=128, bf16, "
+                          f"{nt} tokens ({nt * HKV5 * D5 * 4 / 1e9:.2f} GB K+V) per GPU",
+                "us_per_step": round(ms_b / args.steps * 1e3, 2),
+                "us_per_step_local_only": round(ms_b_local / args.steps * 1e3, 2),
+                "exchange": "all-gather of [1, 32, 129] fp32 partials + LSE merge"
+                            if world > 1 else "none (one GPU)",
+                "correctness_gate_max_abs": err_b},
+        }
+        print(json.dumps(line), flush=True)
+
+
 def run_reference(args) -> None:
     rank, _, world = _env_rank()
     if rank != 0:
@@ -635,8 +797,10 @@ def main() -> None:
     ap.add_argument("--regions", type=int, default=4, help="cold block regions in rotation")
     ap.add_argument("--no-e2e", action="store_true", help="skip the host-buffer e2e leg")
     ap.add_argument("--no-extra", action="store_true", help="skip the config-3 GQA measurement")
-    ap.add_argument("--workload", choices=["config2", "config3", "config4"], default="config2",
-                    help="config3 / config4 run the GQA decode / the prefill alone (profiling)")
+    ap.add_argument("--workload", choices=["config2", "config3", "config4", "config5"],
+                    default="config2",
+                    help="config3 / config4 run the GQA decode / the prefill alone (profiling); "
+                         "config5 the multi-GPU batch-shard + sequence-shard lines (torchrun)")
     ap.add_argument("--ctx-scale", type=int, default=1,
                     help="config3 only: multiply the seeded context lengths (fixed-cost study)")
     ap.add_argument("--pool-blocks", type=int, default=140_000,
@@ -650,6 +814,8 @@ def main() -> None:
         run_config3_only(args)
     elif args.workload == "config4":
         run_config4_only(args)
+    elif args.workload == "config5":
+        run_config5(args)
     else:
         run_b200(args)
 
