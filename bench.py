@@ -603,9 +603,10 @@ def run_config5(args) -> None:
     shard: gpt2 fp16 decode, 64 sequences of ctx 8192 per GPU, `--layers`
     layer pools with 2 cold regions, no collective; (B) one sequence of
     1,048,576 tokens, 32 query / 8 KV heads, D=128, bf16, its token range split
-    evenly over the ranks: each decodes its range (paged_attention_v3_lse),
-    the (out, lse) partials cross NVLink in one all-gather and are merged
-    (pa_b200.dist.sequence_sharded_decode).  Times are the max over ranks;
+    evenly over the ranks: each decodes its range into its exchange buffer and
+    one launch merges the ranks' partials over peer memory
+    (pa_b200.dist.PeerMerge); the NCCL all-gather variant
+    (sequence_sharded_decode) is timed beside it.  Times are the max over ranks;
     the B output is checked against per-rank dense fp32 partials merged with
     the same rule."""
     import datetime
@@ -688,9 +689,14 @@ def run_config5(args) -> None:
     scale5 = D5 ** -0.5
     group = dist.group.WORLD if world > 1 else None
 
+    pm = padist.PeerMerge(1, H5, D5) if world > 1 else None
+
     def decode_b(i: int):
         if world == 1:
             return ops.paged_attention_v3(qb, kv[0], kv[1], btb[i % R5], ctxb, scale5, 0)
+        return pm.decode(qb, kv[0], kv[1], btb[i % R5], ctxb, scale5)
+
+    def decode_b_nccl(i: int):
         return padist.sequence_sharded_decode(qb, kv[0], kv[1], btb[i % R5], ctxb, scale5, group)
 
     # gate: dense fp32 partial of this rank's range, merged over the ranks
@@ -717,15 +723,23 @@ def run_config5(args) -> None:
     else:
         want = o_loc
     err_b = float((got[0] - want).abs().max())
+    if world > 1:
+        err_b = max(err_b, float((decode_b_nccl(0)[0] - want).abs().max()))
+        if int(pm.status.item()) != 0:
+            raise SystemExit(f"config5: device status {int(pm.status.item())}")
     err_b = max_over_ranks(err_b)
     torch.cuda.empty_cache()
 
     ms_b = timed(decode_b, args.steps)
+    ms_b_nccl = timed(decode_b_nccl, args.steps) if world > 1 else ms_b
     # the same decode without the exchange: how much the all-gather + merge add
     ms_b_local = timed(lambda i: ops.paged_attention_v3_lse(qb, kv[0], kv[1], btb[i % R5], ctxb,
                                                             scale5, 0), args.steps)
     bytes_b = NT * HKV5 * D5 * 2 * 2 * args.steps
     if world > 1:
+        if int(pm.status.item()) != 0:
+            raise SystemExit(f"config5: device status {int(pm.status.item())}")
+        pm.close()
         dist.barrier()
         dist.destroy_process_group()
     if rank == 0:
@@ -749,8 +763,9 @@ def run_config5(args) -> None:
                           f"{nt} tokens ({nt * HKV5 * D5 * 4 / 1e9:.2f} GB K+V) per GPU",
                 "us_per_step": round(ms_b / args.steps * 1e3, 2),
                 "us_per_step_local_only": round(ms_b_local / args.steps * 1e3, 2),
-                "exchange": "all-gather of [1, 32, 129] fp32 partials + LSE merge"
-                            if world > 1 else "none (one GPU)",
+                "exchange": "peer memory: flags + peer loads + LSE merge in one launch "
+                            "(pa_merge_peer_partials)" if world > 1 else "none (one GPU)",
+                "us_per_step_nccl_all_gather": round(ms_b_nccl / args.steps * 1e3, 2),
                 "correctness_gate_max_abs": err_b},
         }
         print(json.dumps(line), flush=True)

@@ -27,6 +27,7 @@ PA_ERR_CUDA = 8
 PA_ERR_TOO_LARGE = 9
 PA_ERR_NO_DEVICE = 10
 PA_DEVERR_BLOCK_ID, PA_DEVERR_CONTEXT, PA_DEVERR_TIMEOUT = 1, 2, 4
+PA_IPC_HANDLE_BYTES = 64
 
 _P = ctypes.c_void_p
 _I = ctypes.c_int
@@ -52,6 +53,13 @@ SIGNATURES = {
     "pa_paged_attention_v2": (_I, [_P, _P, _P, _P, _I, _P, _P] + [_I64] * 7 +
                               [_D, _P, _SZ, _P, _P]),
     "pa_merge_states": (_I, [_P, _P, _P, _P, _I64, _I64, _I64, _P]),
+    "pa_peer_exchange_layout": (_I, [_I64, _I64] + [ctypes.POINTER(_SZ)] * 4),
+    "pa_ipc_alloc": (_I, [_SZ, ctypes.POINTER(_P), _P]),
+    "pa_ipc_open": (_I, [_P, ctypes.POINTER(_P)]),
+    "pa_ipc_close": (_I, [_P]),
+    "pa_ipc_free": (_I, [_P]),
+    "pa_merge_peer_partials": (_I, [_P, _P, _P, _I64, _I64, _I64, _I64, ctypes.c_uint32, _P,
+                                    _P]),
     "pa_prefill_workspace_size": (_I, [_I64, _I64, _I64, _I64, _I64, _I, _I64, _I64,
                                        ctypes.POINTER(_SZ)]),
     "pa_paged_attention_prefill": (_I, [_P, _P, _P, _P, _I, _P, _P] + [_I64] * 8 +

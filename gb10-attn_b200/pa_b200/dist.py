@@ -16,9 +16,18 @@ GPU (``torch.distributed``, NCCL over NVLink):
 
 The compute and merge steps are injectable so the host logic (ranges, packing,
 gather order, merge) is testable on CPU ranks with gloo.
+
+``PeerMerge`` is the same sequence-sharded decode with the exchange on peer
+memory instead of a collective: every rank's decode writes its partial into
+an exchange buffer in its own HBM that every other rank has mapped (CUDA IPC),
+and one small kernel of ours (``pa_merge_peer_partials``) raises this rank's
+step flag on every peer, waits (bounded) for theirs and merges the peers'
+partials with plain peer loads -- one launch instead of an all-gather plus a
+merge launch.
 """
 from __future__ import annotations
 
+import ctypes
 from typing import Callable
 
 import torch
@@ -69,3 +78,118 @@ def sequence_sharded_decode(q: torch.Tensor, k_local: torch.Tensor, v_local: tor
     outs, lses = gather_states(out, lse, group)
     merged, _ = merge_fn(outs, lses)
     return merged
+
+
+class PeerMerge:
+    """Sequence-sharded decode with its exchange on peer memory.
+
+    Collective to construct and to ``close()``: every rank of `group` builds
+    one with the same (num_seqs, num_heads, head_dim).  ``decode`` is called
+    once per step on every rank in the same order (each call is one epoch of
+    the exchange protocol of ``include/pa_b200.h``); it returns the merged
+    [B, H, D] output, identical on every rank.  ``status`` is the device
+    word the kernels OR their PA_DEVERR_* bits into (a timed-out exchange
+    wait sets PA_DEVERR_TIMEOUT and yields NaN rows)."""
+
+    def __init__(self, num_seqs: int, num_heads: int, head_dim: int, group=None,
+                 device: torch.device | None = None):
+        from . import _lib
+        self._lib = _lib
+        self.group = group
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        self.dev = device or torch.device("cuda", torch.cuda.current_device())
+        self.B, self.H, self.D = num_seqs, num_heads, head_dim
+        self.rows = num_seqs * num_heads
+        f = [ctypes.c_size_t(0) for _ in range(4)]
+        _lib.check("pa_peer_exchange_layout",
+                   _lib.call("pa_peer_exchange_layout", self.rows, head_dim,
+                             *[ctypes.byref(x) for x in f]))
+        self.lse_offset, self.slot_bytes, self.flags_offset, total = (x.value for x in f)
+        handle = ctypes.create_string_buffer(_lib.PA_IPC_HANDLE_BYTES)
+        base = ctypes.c_void_p(0)
+        with torch.cuda.device(self.dev):
+            _lib.check("pa_ipc_alloc", _lib.call("pa_ipc_alloc", total, ctypes.byref(base),
+                                                 handle))
+        self.base = base.value
+        handles: list = [None] * self.world
+        dist.all_gather_object(handles, handle.raw, group=group)
+        self._opened = []
+        bases = []
+        with torch.cuda.device(self.dev):
+            for r, h in enumerate(handles):
+                if r == self.rank:
+                    bases.append(self.base)
+                    continue
+                p = ctypes.c_void_p(0)
+                _lib.check("pa_ipc_open", _lib.call("pa_ipc_open", h, ctypes.byref(p)))
+                self._opened.append(p.value)
+                bases.append(p.value)
+        as_i64 = [b - (1 << 64) if b >= (1 << 63) else b for b in bases]
+        self.peer_bases = torch.tensor(as_i64, dtype=torch.int64, device=self.dev)
+        self.status = torch.zeros(1, dtype=torch.int32, device=self.dev)
+        self._ws = None
+        self.epoch = 0
+        # every buffer is zeroed (pa_ipc_alloc synchronises) before any rank
+        # can raise a flag in it
+        dist.barrier(group)
+
+    def slot(self, epoch: int) -> tuple[int, int]:
+        """(out, lse) device addresses of this rank's slot for `epoch`."""
+        s = self.base + (epoch & 1) * self.slot_bytes
+        return s, s + self.lse_offset
+
+    def decode(self, q: torch.Tensor, k_local: torch.Tensor, v_local: torch.Tensor,
+               block_tables_local: torch.Tensor, context_lens_local: torch.Tensor,
+               scale: float, out: torch.Tensor | None = None,
+               num_splits: int = 0) -> torch.Tensor:
+        L = self._lib
+        B, H, D = q.shape
+        if (B, H, D) != (self.B, self.H, self.D):
+            raise ValueError(f"PeerMerge built for {(self.B, self.H, self.D)}, got {(B, H, D)}")
+        NB, BS, HKV, _ = k_local.shape
+        MB = block_tables_local.shape[1]
+        dt = {torch.float32: L.PA_DTYPE_F32, torch.float16: L.PA_DTYPE_F16,
+              torch.bfloat16: L.PA_DTYPE_BF16, torch.float64: L.PA_DTYPE_F64}[k_local.dtype]
+        if self._ws is None or self._ws_key != (NB, BS, HKV, MB, dt, num_splits):
+            n = ctypes.c_size_t(0)
+            L.check("pa_decode_workspace_size",
+                    L.call("pa_decode_workspace_size", B, H, HKV, D, dt, BS, MB, num_splits,
+                           ctypes.byref(n)))
+            self._ws = torch.empty(max(n.value, 1), dtype=torch.uint8, device=self.dev)
+            self._ws_bytes = n.value
+            self._ws_key = (NB, BS, HKV, MB, dt, num_splits)
+        qf = q.float().contiguous()
+        if out is None:
+            out = torch.empty((B, H, D), dtype=torch.float32, device=self.dev)
+        stream = torch.cuda.current_stream(self.dev).cuda_stream
+        # u32 serial numbers: after 2^32 - 1 comes 0, which still compares as
+        # newer than the flags of the step before; the parity keeps alternating
+        self.epoch = (self.epoch + 1) & 0xFFFFFFFF
+        o_ptr, l_ptr = self.slot(self.epoch)
+        L.check("pa_paged_attention_v3",
+                L.call("pa_paged_attention_v3", o_ptr, l_ptr, qf.data_ptr(), k_local.data_ptr(),
+                       v_local.data_ptr(), dt, block_tables_local.data_ptr(),
+                       context_lens_local.data_ptr(), B, H, HKV, D, BS, NB, MB, float(scale),
+                       num_splits, self._ws.data_ptr(), self._ws_bytes,
+                       self.status.data_ptr(), stream))
+        L.check("pa_merge_peer_partials",
+                L.call("pa_merge_peer_partials", out.data_ptr(), None,
+                       self.peer_bases.data_ptr(), self.world, self.rank, self.rows, D,
+                       self.epoch, self.status.data_ptr(), stream))
+        return out
+
+    def close(self) -> None:
+        """Collective: unmap the peers' buffers and free this rank's."""
+        if self.base is None:
+            return
+        torch.cuda.synchronize(self.dev)
+        dist.barrier(self.group)  # no rank still reads a peer buffer
+        with torch.cuda.device(self.dev):
+            for p in self._opened:
+                self._lib.check("pa_ipc_close", self._lib.call("pa_ipc_close", p))
+            self._opened = []
+        dist.barrier(self.group)  # every mapping of this rank's buffer is gone
+        with torch.cuda.device(self.dev):
+            self._lib.check("pa_ipc_free", self._lib.call("pa_ipc_free", self.base))
+        self.base = None

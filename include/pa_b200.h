@@ -191,6 +191,45 @@ PA_API int pa_merge_states(float* out, float* lse_out, const float* outs,
                     int64_t head_dim, void* stream);
 
 /* ------------------------------------------------------------------------ */
+/* sequence-sharded decode over peer memory (one process per GPU)           */
+/* ------------------------------------------------------------------------ */
+/* The same merge as pa_merge_states with the partials read straight from the
+ * other GPUs' memory instead of an all-gather.  The reference is single-GPU
+ * (docs/REPORT.md:274); these entry points are additions.
+ *
+ * Each rank allocates one exchange buffer (pa_ipc_alloc, zeroed), sends the
+ * handle to every other rank by any host channel, maps theirs (pa_ipc_open)
+ * and builds a device array peer_bases[world] of every rank's buffer address
+ * in its own address space (its own buffer at index rank).  Layout of a
+ * buffer, from pa_peer_exchange_layout for `rows` = num_seqs * num_heads:
+ *   slot s (s = 0, 1) at s * slot_bytes: out [rows, head_dim] fp32 at +0,
+ *   lse [rows] fp32 at +lse_offset; flags (u32 per rank) at flags_offset.
+ * Step with epoch e (1, 2, 3, ..., the same on every rank, e != 0): the rank's
+ * decode writes its partial (out, lse of its token range, e.g.
+ * pa_paged_attention_v3 with lse) into slot e & 1 of its OWN buffer; then
+ * pa_merge_peer_partials on the same stream raises flag e on every peer,
+ * waits (bounded, 1 s) for every peer's flag e, and writes the merged
+ * out [rows, head_dim] (and lse_out, nullable) on this device.  A wait that
+ * gives up writes NaN rows and ORs PA_DEVERR_TIMEOUT into *dev_status
+ * (nullable).  Every rank must call it once per epoch, in the same order.
+ * world <= 32. */
+#define PA_IPC_HANDLE_BYTES 64
+PA_API int pa_peer_exchange_layout(int64_t rows, int64_t head_dim, size_t* lse_offset,
+                                   size_t* slot_bytes, size_t* flags_offset,
+                                   size_t* total_bytes);
+/* cudaMalloc + zero + an IPC handle (PA_IPC_HANDLE_BYTES bytes) for it. */
+PA_API int pa_ipc_alloc(size_t bytes, void** dev_ptr, void* handle);
+/* Map another process's buffer; returns its address in this process. */
+PA_API int pa_ipc_open(const void* handle, void** dev_ptr);
+PA_API int pa_ipc_close(void* dev_ptr);  /* unmap a pa_ipc_open address   */
+PA_API int pa_ipc_free(void* dev_ptr);   /* free a pa_ipc_alloc buffer    */
+PA_API int pa_merge_peer_partials(float* out, float* lse_out,
+                                  const uint64_t* peer_bases, int64_t world,
+                                  int64_t rank, int64_t rows, int64_t head_dim,
+                                  uint32_t epoch, int32_t* dev_status,
+                                  void* stream);
+
+/* ------------------------------------------------------------------------ */
 /* prefill                                                                   */
 /* ------------------------------------------------------------------------ */
 

@@ -94,6 +94,6 @@ def abi_prefill(q, k, v, bt, ctx, scale, dtype, entry="pa_paged_attention_prefil
 
 def max_abs(a, b) -> float:
     a, b = np.asarray(a, np.float64), np.asarray(b, np.float64)
-    both_nan = np.isnan(a) & np.isnan(b)
-    d = np.abs(np.where(both_nan, 0, a) - np.where(both_nan, 0, b))
+    same = (np.isnan(a) & np.isnan(b)) | (np.isinf(a) & (a == b))  # NaN/NaN, equal infinities
+    d = np.abs(np.where(same, 0, a) - np.where(same, 0, b))
     return float(np.nan_to_num(d, nan=np.inf).max(initial=0.0))

@@ -65,6 +65,38 @@ def test_empty_batch_is_a_no_op():
     assert st == 0
 
 
+def test_peer_exchange_layout_and_argument_checks():
+    f = [ctypes.c_size_t(0) for _ in range(4)]
+    assert _lib.call("pa_peer_exchange_layout", 32, 128, *[ctypes.byref(x) for x in f]) == 0
+    lse_off, slot, flags_off, total = (x.value for x in f)
+    # out [32, 128] fp32, lse [32] fp32, each 256-byte aligned; two slots + flags
+    assert lse_off == 32 * 128 * 4 and slot == lse_off + 256
+    assert flags_off == 2 * slot and total == flags_off + 256  # 32 u32 flags, padded
+    assert _lib.call("pa_peer_exchange_layout", 7, 62, *[ctypes.byref(x) for x in f]) == 0
+    assert f[0].value % 256 == 0 and f[1].value % 256 == 0 and f[0].value >= 7 * 62 * 4
+    assert _lib.call("pa_peer_exchange_layout", -1, 62,
+                     *[ctypes.byref(x) for x in f]) == _lib.PA_ERR_INVALID_ARGUMENT
+    bad = _lib.PA_ERR_INVALID_ARGUMENT
+    dummy = ctypes.c_void_p(16)
+    # world outside [1, 32], rank outside [0, world), null pointers: rejected
+    # before any launch
+    assert _lib.call("pa_merge_peer_partials", dummy, None, dummy, 0, 0, 4, 128, 1, None,
+                     None) == bad
+    assert _lib.call("pa_merge_peer_partials", dummy, None, dummy, 33, 0, 4, 128, 1, None,
+                     None) == bad
+    assert _lib.call("pa_merge_peer_partials", dummy, None, dummy, 2, 2, 4, 128, 1, None,
+                     None) == bad
+    assert _lib.call("pa_merge_peer_partials", None, None, dummy, 2, 0, 4, 128, 1, None,
+                     None) == bad
+    assert _lib.call("pa_merge_peer_partials", dummy, None, None, 2, 0, 4, 128, 1, None,
+                     None) == bad
+    # no rows: nothing to do
+    assert _lib.call("pa_merge_peer_partials", dummy, None, dummy, 2, 1, 0, 128, 1, None,
+                     None) == 0
+    assert _lib.call("pa_ipc_alloc", 0, ctypes.byref(ctypes.c_void_p()), None) == bad
+    assert _lib.call("pa_ipc_open", None, ctypes.byref(ctypes.c_void_p())) == bad
+
+
 def test_write_kv_argument_checks():
     st = _lib.call("pa_write_kv", None, None, _lib.PA_DTYPE_F16, None, None, 9, 0, 0, 0, None,
                    4, 0, 10, 1, 12, 64, 16, 10, None, None)
