@@ -293,7 +293,12 @@ def run_b200(args) -> None:
         torch.cuda.empty_cache()
         line["extra"] = {"config3_gqa_long_context": run_config3(torch, ops, harness, dev,
                                                                  stream, args, peaks),
-                         "config4_prefill": run_config4(torch, ops, harness, dev, stream, args)}
+                         "config4_prefill": run_config4(torch, ops, harness, dev, stream, args),
+                         "fp8_kv_config2_geometry": run_fp8(torch, ops, harness, dev, stream,
+                                                            args, peaks)}
+        fp8 = line["extra"]["fp8_kv_config2_geometry"]
+        fp8["tokens_per_s_vs_fp16_line"] = round(
+            fp8["tokens_per_s"] / line["config"]["tokens_per_s"], 3)
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_baseline(args.cpu_seconds)
     if world > 1:
@@ -363,6 +368,76 @@ def run_config3(torch, ops, harness, dev, stream, args, peaks) -> dict:
             "tokens_per_s": round(B3 / (ms * 1e-3), 1), "correctness_gate_max_abs": err,
             "ctx_scale": int(args.ctx_scale),
             "kernel": "pa::decode::decode_kernel<__nv_bfloat16,128,4> (warp-specialised)"}
+
+
+def run_fp8(torch, ops, harness, dev, stream, args, peaks) -> dict:
+    """The config-2 decode (gpt2, B=64, ctx 2048, 12 layers, 4 cold regions)
+    on an FP8 E4M3 pool with per-KV-head scales (paged_attention_v3_fp8): half
+    the K/V bytes of the fp16 line.  An addition beyond the reference; timed
+    like the headline (device events around the whole loop)."""
+    L, REG = args.layers, args.regions
+    nb = B * (CTX // BS) * REG
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(4321)
+    pools, scales = [], []
+    for _ in range(L):
+        t = torch.empty((2, nb, BS, HKV, D), dtype=torch.float16, device=dev)
+        t.normal_(generator=gen)
+        pools.append(t.to(torch.float8_e4m3fn))
+        del t
+        scales.append(torch.rand((2, HKV), generator=gen, device=dev) * 0.02 + 0.01)
+    q = torch.randn((L, B, H, D), generator=gen, device=dev)
+    ctx = np.full(B, CTX, np.int32)
+    tables = harness.cold_regions([CTX // BS] * B, REG, nb, seed=11)
+    bt = [torch.from_numpy(t).to(dev) for t in tables]
+    ctx_d = torch.from_numpy(ctx).to(dev)
+    scale = D ** -0.5
+    outs = [None] * L
+
+    def call(layer, i):
+        return ops.paged_attention_v3_fp8(q[layer], pools[layer][0], pools[layer][1],
+                                          bt[i % REG], ctx_d, scale, scales[layer][0],
+                                          scales[layer][1], 0)[0]
+
+    # gate: two sequences of layer 0 against dense fp32 on the dequantised pool
+    got = call(0, 0)
+    err = 0.0
+    for b in (0, B - 1):
+        blocks = torch.from_numpy(tables[0][b].astype(np.int64)).to(dev)
+        kk = pools[0][0][blocks].float().reshape(-1, HKV, D) * scales[0][0][None, :, None]
+        vv = pools[0][1][blocks].float().reshape(-1, HKV, D) * scales[0][1][None, :, None]
+        sc = torch.einsum("hd,thd->ht", q[0, b], kk) * scale
+        want = torch.einsum("ht,thd->hd", torch.softmax(sc, -1), vv)
+        err = max(err, float((got[b] - want).abs().max()))
+    if err > 2e-3:
+        raise SystemExit(f"fp8 correctness gate failed: max-abs {err}")
+
+    def step(i):
+        for layer in range(L):
+            outs[layer] = call(layer, i)
+
+    for i in range(args.warmup):
+        step(i)
+    torch.cuda.synchronize()
+    n = max(20, args.steps // 4)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for i in range(n):
+        step(i)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / n
+    per_call = harness.decode_bytes(ctx, H, HKV, D, 1, BS)
+    gbs = L * per_call / (ms * 1e-3) / 1e9
+    del pools, outs
+    torch.cuda.empty_cache()
+    return {"value": round(gbs, 1), "unit": "GB/s",
+            "pct_of_measured_hbm_peak": round(100 * gbs / peaks["hbm_gbs"], 1),
+            "ms_per_step": round(ms, 4), "bytes_per_call": per_call, "steps": n,
+            "tokens_per_s": round(B / (ms * 1e-3), 1), "correctness_gate_max_abs": err,
+            "config": f"configs[1] geometry on an e4m3 pool, {L} layers, {REG} cold regions, "
+                      "per-KV-head scales",
+            "kernel": "pa::decode::decode_kernel<__nv_fp8_e4m3,64,1> (warp-specialised)"}
 
 
 def correctness_gate(torch, layer_call, pool, q, bt_np, bt_dev, ctx_dev, scale, dev) -> float:
@@ -598,6 +673,18 @@ def run_config3_only(args) -> None:
                       "workload": "configs[2]", "detail": r}), flush=True)
 
 
+def run_fp8_only(args) -> None:
+    """--workload fp8: the FP8-pool decode at configs[1] geometry alone."""
+    import torch
+
+    from pa_b200 import harness, ops
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    r = run_fp8(torch, ops, harness, dev, torch.cuda.current_stream(), args, _peaks())
+    print(json.dumps({"metric": METRIC, "value": r["value"], "unit": "GB/s", "n_gpus": 1,
+                      "workload": "configs[1] geometry, e4m3 pool", "detail": r}), flush=True)
+
+
 def run_config5(args) -> None:
     """BASELINE.json configs[4], one process per GPU (torchrun).  (A) batch
     shard: gpt2 fp16 decode, 64 sequences of ctx 8192 per GPU, `--layers`
@@ -812,10 +899,11 @@ def main() -> None:
     ap.add_argument("--regions", type=int, default=4, help="cold block regions in rotation")
     ap.add_argument("--no-e2e", action="store_true", help="skip the host-buffer e2e leg")
     ap.add_argument("--no-extra", action="store_true", help="skip the config-3 GQA measurement")
-    ap.add_argument("--workload", choices=["config2", "config3", "config4", "config5"],
+    ap.add_argument("--workload", choices=["config2", "config3", "config4", "config5", "fp8"],
                     default="config2",
-                    help="config3 / config4 run the GQA decode / the prefill alone (profiling); "
-                         "config5 the multi-GPU batch-shard + sequence-shard lines (torchrun)")
+                    help="config3 / config4 / fp8 run the GQA decode / the prefill / the FP8-pool "
+                         "decode alone (profiling); config5 the multi-GPU batch-shard + "
+                         "sequence-shard lines (torchrun)")
     ap.add_argument("--ctx-scale", type=int, default=1,
                     help="config3 only: multiply the seeded context lengths (fixed-cost study)")
     ap.add_argument("--pool-blocks", type=int, default=140_000,
@@ -831,6 +919,8 @@ def main() -> None:
         run_config4_only(args)
     elif args.workload == "config5":
         run_config5(args)
+    elif args.workload == "fp8":
+        run_fp8_only(args)
     else:
         run_b200(args)
 

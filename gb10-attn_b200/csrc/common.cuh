@@ -5,6 +5,7 @@
 
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
+#include <cuda_fp8.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -21,6 +22,7 @@ template <> struct DTypeId<float> { static constexpr int value = PA_DTYPE_F32; }
 template <> struct DTypeId<__half> { static constexpr int value = PA_DTYPE_F16; };
 template <> struct DTypeId<__nv_bfloat16> { static constexpr int value = PA_DTYPE_BF16; };
 template <> struct DTypeId<double> { static constexpr int value = PA_DTYPE_F64; };
+template <> struct DTypeId<__nv_fp8_e4m3> { static constexpr int value = PA_DTYPE_E4M3; };
 
 inline int dtype_size(int dt) {
   switch (dt) {
@@ -28,6 +30,7 @@ inline int dtype_size(int dt) {
     case PA_DTYPE_F16: return 2;
     case PA_DTYPE_BF16: return 2;
     case PA_DTYPE_F64: return 8;
+    case PA_DTYPE_E4M3: return 1;
     default: return 0;
   }
 }
@@ -58,6 +61,27 @@ template <> struct Chunk<__nv_bfloat16> {
     for (int i = 0; i < 4; ++i) {
       f[2 * i] = __uint_as_float(w[i] << 16);
       f[2 * i + 1] = __uint_as_float(w[i] & 0xffff0000u);
+    }
+  }
+};
+
+template <> struct Chunk<__nv_fp8_e4m3> {
+  static constexpr int N = 16;
+  // e4m3 -> fp16 is exact (every e4m3 value is an fp16 value), then fp16 -> fp32.
+  static __device__ __forceinline__ void cvt(const uint4& u, float* f) {
+    const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const __half2_raw lo =
+          __nv_cvt_fp8x2_to_halfraw2((__nv_fp8x2_storage_t)(w[i] & 0xffffu), __NV_E4M3);
+      const __half2_raw hi =
+          __nv_cvt_fp8x2_to_halfraw2((__nv_fp8x2_storage_t)(w[i] >> 16), __NV_E4M3);
+      const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&lo));
+      const float2 b = __half22float2(*reinterpret_cast<const __half2*>(&hi));
+      f[4 * i] = a.x;
+      f[4 * i + 1] = a.y;
+      f[4 * i + 2] = b.x;
+      f[4 * i + 3] = b.y;
     }
   }
 };

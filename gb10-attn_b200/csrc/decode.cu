@@ -1,7 +1,7 @@
 // decode.cu -- host side of the split-KV decode: configuration choice, the
 // plan kernel (per-call work split), launch of the persistent decode kernel
 // with programmatic dependent launch, and the decode entry points of the C ABI
-// (pa_paged_attention, _v2, _v3, pa_choose_num_splits,
+// (pa_paged_attention, _v2, _v3, _v3_fp8, pa_choose_num_splits,
 // pa_decode_workspace_size, pa_merge_states, pa_validate_block_tables).
 #include <algorithm>
 #include <atomic>
@@ -19,6 +19,7 @@ const void* decode_kernel_ptr_f16(int D, int QC);
 const void* decode_kernel_ptr_bf16(int D, int QC);
 const void* decode_kernel_ptr_f32(int D, int QC);
 const void* decode_kernel_ptr_f64(int D, int QC);
+const void* decode_kernel_ptr_e4m3(int D, int QC);
 
 const void* decode_kernel_ptr(int dtype, int D, int QC) {
   switch (dtype) {
@@ -26,6 +27,7 @@ const void* decode_kernel_ptr(int dtype, int D, int QC) {
     case PA_DTYPE_BF16: return decode_kernel_ptr_bf16(D, QC);
     case PA_DTYPE_F32: return decode_kernel_ptr_f32(D, QC);
     case PA_DTYPE_F64: return decode_kernel_ptr_f64(D, QC);
+    case PA_DTYPE_E4M3: return decode_kernel_ptr_e4m3(D, QC);
     default: return nullptr;
   }
 }
@@ -41,11 +43,11 @@ int decode_elems_per_lane(int dtype, int D) {
 // Returns the CTA kind (decode::CtaKind) of an instantiation.
 static int decode_kind(int dtype, int D, int QC) {
   const int s = QC * decode_elems_per_lane(dtype, D);
-  if (dtype_size(dtype) == 2) return s <= 8 ? 0 : (s <= 32 ? 1 : 2);
+  if (dtype_size(dtype) <= 2) return s <= (dtype_size(dtype) == 1 ? 16 : 8) ? 0 : (s <= 32 ? 1 : 2);
   return s <= 4 ? 0 : (s <= 16 ? 1 : 2);
 }
 static int decode_qc_cap(int dtype) {
-  return dtype_size(dtype) == 2 ? 64 : (dtype_size(dtype) == 4 ? 32 : 16);
+  return dtype_size(dtype) <= 2 ? 64 : (dtype_size(dtype) == 4 ? 32 : 16);
 }
 int decode_max_warps(int dtype, int D, int QC) { return decode_kind(dtype, D, QC) == 2 ? 8 : 16; }
 
@@ -413,6 +415,8 @@ int launch(const DecodeArgs& a, void* ws, size_t ws_bytes, cudaStream_t stream) 
   p.N = c.N;
   p.nstage = c.nstage;
   p.qscale = (float)a.scale * kLog2e;
+  p.k_scale = a.k_scale;
+  p.v_scale = a.v_scale;
   p.row_bytes = c.row_bytes;
   p.rows_contiguous = (c.G == a.HKV) ? 1 : 0;
   const int elt = dtype_size(a.dtype);
@@ -536,8 +540,11 @@ static int decode_entry(float* out, float* lse, const float* q, const void* k, c
                         int dt, const int32_t* bt, const int32_t* ctx, int64_t B, int64_t H,
                         int64_t HKV, int64_t D, int64_t BS, int64_t NB, int64_t MB,
                         double scale, int64_t num_splits, void* ws, size_t ws_bytes,
-                        int32_t* dev_status, void* stream) {
+                        int32_t* dev_status, void* stream, const float* k_scale = nullptr,
+                        const float* v_scale = nullptr) {
   DecodeArgs a;
+  a.k_scale = k_scale;
+  a.v_scale = v_scale;
   a.out = out;
   a.lse = lse;
   a.q = q;
@@ -573,6 +580,24 @@ extern "C" int pa_paged_attention_v3(float* out, float* lse, const float* q, con
                       num_seqs, num_heads, num_kv_heads, head_dim, block_size, num_blocks,
                       max_blocks, scale, num_splits, workspace, workspace_bytes, dev_status,
                       stream);
+}
+
+extern "C" int pa_paged_attention_v3_fp8(float* out, float* lse, const float* q,
+                                         const void* k_cache, const void* v_cache,
+                                         const float* k_scale, const float* v_scale,
+                                         int kv_dtype, const int32_t* block_tables,
+                                         const int32_t* context_lens, int64_t num_seqs,
+                                         int64_t num_heads, int64_t num_kv_heads,
+                                         int64_t head_dim, int64_t block_size,
+                                         int64_t num_blocks, int64_t max_blocks, double scale,
+                                         int64_t num_splits, void* workspace,
+                                         size_t workspace_bytes, int32_t* dev_status,
+                                         void* stream) {
+  if (kv_dtype != PA_DTYPE_E4M3) return PA_ERR_DTYPE;
+  return decode_entry(out, lse, q, k_cache, v_cache, kv_dtype, block_tables, context_lens,
+                      num_seqs, num_heads, num_kv_heads, head_dim, block_size, num_blocks,
+                      max_blocks, scale, num_splits, workspace, workspace_bytes, dev_status,
+                      stream, k_scale, v_scale);
 }
 
 extern "C" int pa_paged_attention(float* out, const float* q, const void* k_cache,

@@ -25,6 +25,8 @@ struct DecodeArgs {
   int32_t* dev_status;
   int64_t qlen = 1;        // query rows per sequence (causal prefill: Sq)
   float empty_fill = 0.f;  // value of rows that see no key
+  const float* k_scale = nullptr;  // FP8 pools: [HKV] dequantisation scales (null = 1)
+  const float* v_scale = nullptr;
 };
 
 int launch(const DecodeArgs& a, void* ws, size_t ws_bytes, cudaStream_t stream);

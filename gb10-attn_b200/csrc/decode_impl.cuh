@@ -81,6 +81,10 @@ struct Params {
   int64_t qlen;
   int32_t G, QPK, NS, NGC, N, nstage;
   float qscale;                  // scale * log2(e)
+  // FP8 pools: per-KV-head dequantisation scales (null = 1); K's scale folds
+  // into q, V's into the softmax weights.  Unused for the other dtypes.
+  const float* k_scale;
+  const float* v_scale;
   uint32_t row_bytes;            // G * D * sizeof(T)
   int32_t rows_contiguous;       // G == HKV: a page's token rows are adjacent
   int64_t tok_stride;            // HKV * D * sizeof(T): one token row of a page
@@ -109,8 +113,8 @@ struct Geo {
 
 // CTA shape of a (T, D, QC) instantiation, by the per-lane register state
 // S = QC * EPL floats of q (and as many of acc):
-//  * kLight (S <= 8, or <= 4 for 4/8-byte types): consumer warps 0..NS-1 (up
-//    to 16) plus the producer warp NS; (NS + 1) * 32 threads.
+//  * kLight (S <= 8; <= 16 for FP8; <= 4 for 4/8-byte types): consumer warps
+//    0..NS-1 (up to 16) plus the producer warp NS; (NS + 1) * 32 threads.
 //  * kWs16 (S <= 32): warp-specialised.  Warpgroup 0 is the producer (warp 0
 //    issues copies, warps 1-3 retire) and hands registers back with
 //    setmaxnreg.dec; warpgroups 1-4 are up to 16 consumer warps.  640 threads
@@ -126,7 +130,10 @@ enum CtaKind { kLight = 0, kWs16 = 1, kWs8 = 2 };
 template <typename T, int D, int QC>
 struct Limits {
   static constexpr int S = QC * Geo<T, D>::EPL;
-  static constexpr int KIND = (sizeof(T) == 2 ? (S <= 8 ? kLight : (S <= 32 ? kWs16 : kWs8))
+  // FP8 rows put 16 elements in a lane at D = 64: still a light CTA (measured
+  // 3.28 TB/s at configs[1] geometry, against 2.67 TB/s as a kWs16 CTA)
+  static constexpr int kLightS = sizeof(T) == 1 ? 16 : 8;
+  static constexpr int KIND = (sizeof(T) <= 2 ? (S <= kLightS ? kLight : (S <= 32 ? kWs16 : kWs8))
                                               : (S <= 4 ? kLight : (S <= 16 ? kWs16 : kWs8)));
   static constexpr bool WS = KIND != kLight;
   static constexpr int MAXW = KIND == kWs8 ? 8 : 16;
@@ -718,6 +725,7 @@ __global__ void __launch_bounds__(Limits<T, D, QC>::THREADS, 1)
   int64_t seg_gt0 = 0;
   int b = 0, gc = 0;
   int64_t head0 = 0;
+  float vsc = 1.f;  // FP8 pools: V's dequantisation scale for this KV head
 
   while (true) {
     if (!mbar_wait(&full[stage], phase, p.abort_flag, p.abort_tag)) {
@@ -736,6 +744,12 @@ __global__ void __launch_bounds__(Limits<T, D, QC>::THREADS, 1)
       seg_gt0 = h.gt;
       head0 = ((int64_t)gc * p.G + g_local) * p.QPK + hq0;
       const float* qp = p.q + ((int64_t)b * p.H + head0) * D;
+      float qs = p.qscale;
+      if constexpr (sizeof(T) == 1) {
+        const int64_t kvh = (int64_t)gc * p.G + g_local;
+        if (p.k_scale) qs *= p.k_scale[kvh];
+        vsc = p.v_scale ? p.v_scale[kvh] : 1.f;
+      }
 #pragma unroll
       for (int j = 0; j < QC; ++j) {
 #pragma unroll
@@ -744,8 +758,8 @@ __global__ void __launch_bounds__(Limits<T, D, QC>::THREADS, 1)
 #pragma unroll
           for (int v = 0; v < VEC; v += 2) {
             const float2 x = *reinterpret_cast<const float2*>(src + v);
-            qf[j][c * VEC + v] = x.x * p.qscale;
-            qf[j][c * VEC + v + 1] = x.y * p.qscale;
+            qf[j][c * VEC + v] = x.x * qs;
+            qf[j][c * VEC + v + 1] = x.y * qs;
           }
         }
         m[j] = kNegBig;
@@ -823,7 +837,9 @@ __global__ void __launch_bounds__(Limits<T, D, QC>::THREADS, 1)
 #pragma unroll
       for (int i = 0; i < TPR; ++i) {
         const float pv = (rg + i * NRG < nvalid) ? fast_exp2(s[i][j] - m[j]) : 0.f;
-        s[i][j] = pv;
+        // FP8: the weight that multiplies the raw V row carries V's scale;
+        // the denominator does not
+        s[i][j] = sizeof(T) == 1 ? pv * vsc : pv;
         lsum += pv;
       }
       l[j] += lsum;
@@ -951,7 +967,7 @@ namespace decode {
 
 template <typename T, int D, int QC>
 const void* kernel_if_fits() {
-  if constexpr (QC * Geo<T, D>::EPL <= (sizeof(T) == 2 ? 64 : (sizeof(T) == 4 ? 32 : 16))) {
+  if constexpr (QC * Geo<T, D>::EPL <= (sizeof(T) <= 2 ? 64 : (sizeof(T) == 4 ? 32 : 16))) {
     return reinterpret_cast<const void*>(&decode_kernel<T, D, QC>);
   } else {
     return nullptr;

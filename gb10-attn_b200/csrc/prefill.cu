@@ -70,6 +70,7 @@ extern "C" int pa_prefill_workspace_size(int64_t num_seqs, int64_t num_queries,
   if (!bytes) return PA_ERR_INVALID_ARGUMENT;
   int st = pa::prefill_checks(num_seqs, num_queries, num_heads, num_kv_heads, head_dim);
   if (st) return st;
+  if (kv_dtype == PA_DTYPE_E4M3) return PA_ERR_DTYPE;  // FP8 pools: decode only
   if (num_seqs == 0 || num_queries == 0) {
     *bytes = 0;
     return PA_OK;
@@ -88,6 +89,7 @@ extern "C" int pa_paged_attention_prefill_simt(
     size_t workspace_bytes, int32_t* dev_status, void* stream) {
   int st = pa::prefill_checks(num_seqs, num_queries, num_heads, num_kv_heads, head_dim);
   if (st) return st;
+  if (kv_dtype == PA_DTYPE_E4M3) return PA_ERR_DTYPE;  // FP8 pools: decode only
   if (num_seqs == 0 || num_queries == 0) return PA_OK;
   pa::decode::DecodeArgs a = pa::prefill_args(
       out, q, k_cache, v_cache, kv_dtype, block_tables, context_lens, num_seqs, num_queries,
@@ -107,6 +109,7 @@ extern "C" int pa_paged_attention_prefill(float* out, const float* q, const void
                                           void* stream) {
   int st = pa::prefill_checks(num_seqs, num_queries, num_heads, num_kv_heads, head_dim);
   if (st) return st;
+  if (kv_dtype == PA_DTYPE_E4M3) return PA_ERR_DTYPE;  // FP8 pools: decode only
   if (num_seqs == 0 || num_queries == 0) return PA_OK;
   if (pa::prefill::tc_eligible(kv_dtype, head_dim, block_size, num_blocks))
     return pa::prefill::launch_tc(out, q, k_cache, v_cache, kv_dtype, block_tables, context_lens,

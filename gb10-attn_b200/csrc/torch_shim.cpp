@@ -15,7 +15,8 @@
 //   paged_attention_prefill_wmma(...)             kernels/paged_attn_wmma.h:13-15
 //
 // plus the pool writer and helpers the reference keeps in Python
-// (write_kv, validate_block_tables, paged_attention_v3_lse, merge_states).
+// (write_kv, validate_block_tables, paged_attention_v3_lse, merge_states), and
+// the FP8-pool additions (paged_attention_v3_fp8, write_kv_scaled).
 //
 // Differences, all supersets: bf16 pools are accepted (the reference's
 // AT_DISPATCH_FLOATING_TYPES_AND_HALF has fp32/fp64/fp16 only); launches go to
@@ -37,6 +38,7 @@ int pool_dtype(const torch::Tensor& t, const char* op) {
     case torch::kHalf: return PA_DTYPE_F16;
     case torch::kBFloat16: return PA_DTYPE_BF16;
     case torch::kDouble: return PA_DTYPE_F64;
+    case torch::kFloat8_e4m3fn: return PA_DTYPE_E4M3;
     default:
       TORCH_CHECK(false, "\"", op, "\" not implemented for '", toString(t.scalar_type()), "'");
   }
@@ -182,6 +184,42 @@ std::tuple<torch::Tensor, torch::Tensor> paged_attention_v3_lse(
                      true);
 }
 
+// Decode of an FP8 (float8_e4m3fn) pool with per-KV-head fp32 scales
+// (K = k_cache * k_scale[h], V = v_cache * v_scale[h]); returns (out, lse).
+// An addition: the reference has no FP8 pool.
+std::tuple<torch::Tensor, torch::Tensor> paged_attention_v3_fp8(
+    torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_cache, torch::Tensor block_tables,
+    torch::Tensor context_lens, double scale, torch::Tensor k_scale, torch::Tensor v_scale,
+    int64_t num_splits) {
+  const char* op = "paged_attention_v3_fp8";
+  TORCH_CHECK(k_cache.scalar_type() == torch::kFloat8_e4m3fn,
+              op, ": k_cache must be float8_e4m3fn");
+  DecodeInputs in = prepare(q, k_cache, v_cache, block_tables, context_lens, op, 3);
+  decode_checks(in);
+  const c10::cuda::CUDAGuard guard(in.q.device());
+  torch::Tensor ks = k_scale.to(in.q.device(), torch::kFloat).contiguous();
+  torch::Tensor vs = v_scale.to(in.q.device(), torch::kFloat).contiguous();
+  TORCH_CHECK(ks.numel() == in.HKV && vs.numel() == in.HKV, op,
+              ": k_scale and v_scale need one entry per KV head");
+  auto fopts = in.q.options().dtype(torch::kFloat32);
+  torch::Tensor out = torch::empty({in.B, in.H, in.D}, fopts);
+  torch::Tensor lse = torch::empty({in.B, in.H}, fopts);
+  if (in.B == 0) return {out, lse};
+  size_t ws_bytes = 0;
+  check_status(pa_decode_workspace_size(in.B, in.H, in.HKV, in.D, in.dtype, in.BS, in.MB,
+                                        num_splits, &ws_bytes),
+               op);
+  torch::Tensor ws = workspace(ws_bytes, in.q);
+  check_status(pa_paged_attention_v3_fp8(
+                   out.data_ptr<float>(), lse.data_ptr<float>(), in.q.data_ptr<float>(),
+                   in.k.data_ptr(), in.v.data_ptr(), ks.data_ptr<float>(), vs.data_ptr<float>(),
+                   in.dtype, in.bt.data_ptr<int32_t>(), in.ctx.data_ptr<int32_t>(), in.B, in.H,
+                   in.HKV, in.D, in.BS, in.NB, in.MB, scale, num_splits, ws.data_ptr(),
+                   ws_bytes, nullptr, stream_ptr()),
+               op);
+  return {out, lse};
+}
+
 int64_t choose_num_splits(int64_t num_seqs, int64_t num_heads, int64_t max_context) {
   const int64_t s = pa_choose_num_splits(num_seqs, num_heads, max_context);
   TORCH_CHECK(s > 0, "choose_num_splits: ", pa_strerror(PA_ERR_NO_DEVICE));
@@ -257,9 +295,11 @@ torch::Tensor paged_attention_prefill_simt(torch::Tensor q, torch::Tensor k_cach
 // per layer); k, v are [n_layer, HKV, n_tok, D] device tensors (head_dim
 // contiguous).  Token t goes to position start + t of the sequence whose
 // pages are block_ids.
-void write_kv(std::vector<torch::Tensor> k_layers, std::vector<torch::Tensor> v_layers,
-              torch::Tensor block_ids, int64_t start, torch::Tensor k, torch::Tensor v) {
-  const char* op = "write_kv";
+// k_scales / v_scales (FP8 pools): [n_layer, HKV] fp32, stored value = x / scale.
+void write_kv_impl(std::vector<torch::Tensor> k_layers, std::vector<torch::Tensor> v_layers,
+                   torch::Tensor block_ids, int64_t start, torch::Tensor k, torch::Tensor v,
+                   c10::optional<torch::Tensor> k_scales, c10::optional<torch::Tensor> v_scales,
+                   const char* op) {
   TORCH_CHECK(!k_layers.empty() && k_layers.size() == v_layers.size(),
               "write_kv: need one K and one V tensor per layer");
   TORCH_CHECK(k.dim() == 4 && v.sizes() == k.sizes(), "write_kv: k, v must be [L, H, T, D]");
@@ -299,12 +339,32 @@ void write_kv(std::vector<torch::Tensor> k_layers, std::vector<torch::Tensor> v_
   torch::Tensor ids = block_ids.to(k0.device(), torch::kInt32).contiguous();
   TORCH_CHECK(kd.size(1) == k0.size(2) && kd.size(3) == k0.size(3),
               "write_kv: k heads / head_dim must match the pool");
-  const int st = pa_write_kv(kp.data(), vp.data(), pdt, kd.data_ptr(), vd.data_ptr(), sdt,
-                             kd.stride(0), kd.stride(1), kd.stride(2), ids.data_ptr<int32_t>(),
-                             ids.numel(), start, kd.size(2), (int64_t)k_layers.size(),
-                             k0.size(2), k0.size(3), k0.size(1), k0.size(0), nullptr,
-                             stream_ptr());
+  torch::Tensor ks, vs;
+  const int64_t L = (int64_t)k_layers.size();
+  for (auto [src, dst] : {std::make_pair(&k_scales, &ks), std::make_pair(&v_scales, &vs)}) {
+    if (!src->has_value()) continue;
+    *dst = src->value().to(k0.device(), torch::kFloat).contiguous();
+    TORCH_CHECK(dst->numel() == L * k0.size(2), op, ": scales must be [n_layer, HKV]");
+  }
+  const int st = pa_write_kv_scaled(
+      kp.data(), vp.data(), pdt, kd.data_ptr(), vd.data_ptr(), sdt, kd.stride(0), kd.stride(1),
+      kd.stride(2), ids.data_ptr<int32_t>(), ids.numel(), start, kd.size(2), L, k0.size(2),
+      k0.size(3), k0.size(1), k0.size(0), ks.defined() ? ks.data_ptr<float>() : nullptr,
+      vs.defined() ? vs.data_ptr<float>() : nullptr, nullptr, stream_ptr());
   check_status(st, op);
+}
+
+void write_kv(std::vector<torch::Tensor> k_layers, std::vector<torch::Tensor> v_layers,
+              torch::Tensor block_ids, int64_t start, torch::Tensor k, torch::Tensor v) {
+  write_kv_impl(std::move(k_layers), std::move(v_layers), block_ids, start, k, v,
+                c10::nullopt, c10::nullopt, "write_kv");
+}
+
+void write_kv_scaled(std::vector<torch::Tensor> k_layers, std::vector<torch::Tensor> v_layers,
+                     torch::Tensor block_ids, int64_t start, torch::Tensor k, torch::Tensor v,
+                     torch::Tensor k_scales, torch::Tensor v_scales) {
+  write_kv_impl(std::move(k_layers), std::move(v_layers), block_ids, start, k, v, k_scales,
+                v_scales, "write_kv_scaled");
 }
 
 // Counts of (out-of-range block ids, over-long contexts); synchronises.
@@ -352,6 +412,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("paged_attention_prefill_wmma", &paged_attention_prefill_wmma);
   m.def("paged_attention_prefill_simt", &paged_attention_prefill_simt);
   m.def("write_kv", &write_kv);
+  m.def("write_kv_scaled", &write_kv_scaled);
+  m.def("paged_attention_v3_fp8", &paged_attention_v3_fp8);
   m.def("validate_block_tables", &validate_block_tables);
   m.def("merge_states", &merge_states);
 }

@@ -1,11 +1,12 @@
-// write_kv.cu -- KV-pool writer (C ABI pa_write_kv).
+// write_kv.cu -- KV-pool writer (C ABI pa_write_kv, pa_write_kv_scaled).
 //
 // Replaces hetero-serve TorchBlockAllocator.write_kv(block_ids, start, k, v)
 // (heteroserve/kv/torch_blocks.py:92, un-vendored; behaviour from the call
 // sites harness/repro_crash.py:52-58 and gb10-attn docs/REPORT.md:141-179):
 // token t of the source, at sequence position p = start + t, goes to row
 // p % BS of block block_ids[p / BS] of every layer's K and V pool, for every
-// kv head, converted to the pool dtype with round-to-nearest-even.
+// kv head, converted to the pool dtype with round-to-nearest-even (FP8 E4M3
+// pools: x / scale[layer, head] first, saturating at +-448; an addition).
 //
 // The reference did this with torch indexing on one [n_layer, 2, NB, BS, H, D]
 // tensor and faulted once that tensor passed 2^31 elements
@@ -33,6 +34,9 @@ struct Params {
   const int32_t* block_ids;
   int64_t n_ids;
   int64_t start, T, L, HKV, D, BS, NB;
+  // FP8 pools: [L, HKV] quantisation scales (null = 1); this launch's layers
+  const float* k_scales;
+  const float* v_scales;
   int32_t* dev_status;
 };
 
@@ -51,6 +55,12 @@ template <> __device__ __forceinline__ double from_f32<double>(float x) { return
 template <> __device__ __forceinline__ __half from_f32<__half>(float x) { return __float2half_rn(x); }
 template <> __device__ __forceinline__ __nv_bfloat16 from_f32<__nv_bfloat16>(float x) {
   return __float2bfloat16_rn(x);
+}
+// round to nearest even, saturating to the largest finite e4m3 (+-448)
+template <> __device__ __forceinline__ __nv_fp8_e4m3 from_f32<__nv_fp8_e4m3>(float x) {
+  __nv_fp8_e4m3 r;
+  r.__x = __nv_cvt_float_to_fp8(x, __NV_SATFINITE, __NV_E4M3);
+  return r;
 }
 
 // VEC: 8 elements per thread with vector loads/stores (needs D % 8 == 0 and
@@ -87,6 +97,11 @@ __global__ void __launch_bounds__(256) write_kv_kernel(const __grid_constant__ P
                    h * p.src_head_stride + t * p.src_token_stride + chunk * E;
     P* dst = reinterpret_cast<P*>(kv ? p.v_layers[l] : p.k_layers[l]) +
              ((blk * p.BS + (pos - page * p.BS)) * p.HKV + h) * p.D + chunk * E;
+    float qs = 1.f;  // FP8: stored value = x / scale
+    if constexpr (sizeof(P) == 1) {
+      const float* sc = kv ? p.v_scales : p.k_scales;
+      if (sc) qs = sc[l * p.HKV + h];
+    }
     if constexpr (VEC) {
       float f[8];
       if constexpr (sizeof(S) == 4) {
@@ -100,7 +115,13 @@ __global__ void __launch_bounds__(256) write_kv_kernel(const __grid_constant__ P
 #pragma unroll
         for (int e = 0; e < 8; ++e) f[e] = to_f32<S>(s8[e]);
       }
-      if constexpr (sizeof(P) == 2) {
+      if constexpr (sizeof(P) == 1) {
+        uint2 u;
+        P* d8 = reinterpret_cast<P*>(&u);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) d8[e] = from_f32<P>(__fdiv_rn(f[e], qs));
+        *reinterpret_cast<uint2*>(dst) = u;
+      } else if constexpr (sizeof(P) == 2) {
         uint4 u;
         P* d8 = reinterpret_cast<P*>(&u);
 #pragma unroll
@@ -115,7 +136,10 @@ __global__ void __launch_bounds__(256) write_kv_kernel(const __grid_constant__ P
           reinterpret_cast<double2*>(dst)[e / 2] = make_double2((double)f[e], (double)f[e + 1]);
       }
     } else {
-      *dst = from_f32<P>(to_f32<S>(*src));
+      if constexpr (sizeof(P) == 1)
+        *dst = from_f32<P>(__fdiv_rn(to_f32<S>(*src), qs));
+      else
+        *dst = from_f32<P>(to_f32<S>(*src));
     }
   }
 }
@@ -142,6 +166,7 @@ static int launch_src(const Params& p, int pool_dtype, bool vec, cudaStream_t s)
     case PA_DTYPE_BF16: return launch_typed<S, __nv_bfloat16>(p, vec, s);
     case PA_DTYPE_F32: return launch_typed<S, float>(p, vec, s);
     case PA_DTYPE_F64: return launch_typed<S, double>(p, vec, s);
+    case PA_DTYPE_E4M3: return launch_typed<S, __nv_fp8_e4m3>(p, vec, s);
     default: return PA_ERR_DTYPE;
   }
 }
@@ -157,6 +182,22 @@ extern "C" int pa_write_kv(void* const* k_layers, void* const* v_layers, int poo
                            int64_t num_layers, int64_t num_kv_heads, int64_t head_dim,
                            int64_t block_size, int64_t num_blocks, int32_t* dev_status,
                            void* stream) {
+  return pa_write_kv_scaled(k_layers, v_layers, pool_dtype, k_src, v_src, src_dtype,
+                            src_layer_stride, src_head_stride, src_token_stride, block_ids,
+                            num_block_ids, start, num_tokens, num_layers, num_kv_heads,
+                            head_dim, block_size, num_blocks, nullptr, nullptr, dev_status,
+                            stream);
+}
+
+extern "C" int pa_write_kv_scaled(void* const* k_layers, void* const* v_layers, int pool_dtype,
+                                  const void* k_src, const void* v_src, int src_dtype,
+                                  int64_t src_layer_stride, int64_t src_head_stride,
+                                  int64_t src_token_stride, const int32_t* block_ids,
+                                  int64_t num_block_ids, int64_t start, int64_t num_tokens,
+                                  int64_t num_layers, int64_t num_kv_heads, int64_t head_dim,
+                                  int64_t block_size, int64_t num_blocks,
+                                  const float* k_scales, const float* v_scales,
+                                  int32_t* dev_status, void* stream) {
   using namespace pa;
   using writekv::kMaxLayers;
   if (num_tokens < 0 || num_layers < 0 || num_kv_heads <= 0 || head_dim <= 0 ||
@@ -195,6 +236,8 @@ extern "C" int pa_write_kv(void* const* k_layers, void* const* v_layers, int poo
     p.D = head_dim;
     p.BS = block_size;
     p.NB = num_blocks;
+    p.k_scales = k_scales ? k_scales + l0 * num_kv_heads : nullptr;
+    p.v_scales = v_scales ? v_scales + l0 * num_kv_heads : nullptr;
     p.dev_status = dev_status;
     int st;
     switch (src_dtype) {

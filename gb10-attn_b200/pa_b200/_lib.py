@@ -14,7 +14,7 @@ PKG_DIR = Path(__file__).resolve().parent
 LIB_PATH = PKG_DIR / "libpa_b200.so"
 HEADER = PKG_DIR.parent.parent / "include" / "pa_b200.h"
 
-PA_DTYPE_F32, PA_DTYPE_F16, PA_DTYPE_BF16, PA_DTYPE_F64 = 0, 1, 2, 3
+PA_DTYPE_F32, PA_DTYPE_F16, PA_DTYPE_BF16, PA_DTYPE_F64, PA_DTYPE_E4M3 = 0, 1, 2, 3, 4
 PA_OK = 0
 PA_ERR_INVALID_ARGUMENT = 1
 PA_ERR_NUM_HEADS = 2
@@ -48,6 +48,8 @@ SIGNATURES = {
                               [_D, _I64, _P, _SZ, _P, _P]),
     "pa_paged_attention_v3_noalloc": (_I, [_P, _P, _P, _P, _P, _I, _P, _P] + [_I64] * 7 +
                                       [_D, _I64, _P, _P]),
+    "pa_paged_attention_v3_fp8": (_I, [_P, _P, _P, _P, _P, _P, _P, _I, _P, _P] + [_I64] * 7 +
+                                  [_D, _I64, _P, _SZ, _P, _P]),
     "pa_paged_attention": (_I, [_P, _P, _P, _P, _I, _P, _P] + [_I64] * 7 +
                            [_D, _P, _SZ, _P, _P]),
     "pa_paged_attention_v2": (_I, [_P, _P, _P, _P, _I, _P, _P] + [_I64] * 7 +
@@ -70,6 +72,8 @@ SIGNATURES = {
                                         [_D, _P, _SZ, _P, _P]),
     "pa_write_kv": (_I, [_P, _P, _I, _P, _P, _I, _I64, _I64, _I64, _P] + [_I64] * 8 +
                     [_P, _P]),
+    "pa_write_kv_scaled": (_I, [_P, _P, _I, _P, _P, _I, _I64, _I64, _I64, _P] + [_I64] * 8 +
+                           [_P, _P, _P, _P]),
     "pa_validate_block_tables": (_I, [_P, _P, _I64, _I64, _I64, _I64, _P, _P]),
 }
 

@@ -32,7 +32,8 @@ INT32_MAX = 2**31 - 1
 
 _DTYPES = {"float16": torch.float16, "bfloat16": torch.bfloat16, "float32": torch.float32,
            "float64": torch.float64, "half": torch.float16, "bf16": torch.bfloat16,
-           "float": torch.float32}
+           "float": torch.float32, "e4m3": torch.float8_e4m3fn,
+           "float8_e4m3fn": torch.float8_e4m3fn}
 
 
 @dataclass
@@ -134,14 +135,39 @@ class TorchBlockAllocator:
         dt = _DTYPES[kv_cfg.dtype] if isinstance(kv_cfg.dtype, str) else kv_cfg.dtype
         m = self.model_cfg
         per_layer = (2, kv_cfg.num_blocks, kv_cfg.block_size, m.kv_heads, m.head_dim)
-        make = torch.zeros if zero else torch.empty
+        self.fp8 = dt == torch.float8_e4m3fn
+
+        def make(shape):
+            if self.fp8:  # bytes, viewed as e4m3 (zero bytes are +0.0)
+                t = (torch.zeros if zero else torch.empty)(shape, dtype=torch.uint8,
+                                                           device=self.device)
+                return t.view(dt)
+            return (torch.zeros if zero else torch.empty)(shape, dtype=dt, device=self.device)
+
         self.layered = layered
         if layered:
-            self.pool = LayeredPool([make(per_layer, dtype=dt, device=self.device)
-                                     for _ in range(m.n_layer)])
+            self.pool = LayeredPool([make(per_layer) for _ in range(m.n_layer)])
         else:
-            self.pool = make((m.n_layer, *per_layer), dtype=dt, device=self.device)
+            self.pool = make((m.n_layer, *per_layer))
+        # FP8 pools: per-(layer, kv head) scales, stored value = x / scale
+        self.k_scales = self.v_scales = None
+        if self.fp8:
+            self.k_scales = torch.ones((m.n_layer, m.kv_heads), dtype=torch.float32,
+                                       device=self.device)
+            self.v_scales = torch.ones_like(self.k_scales)
         self._free = list(range(kv_cfg.num_blocks - 1, -1, -1))
+
+    def set_scales(self, k_scales, v_scales) -> None:
+        """FP8 pools: the [n_layer, n_kv_head] quantisation scales used by
+        write_kv (and to be passed to the decode with ``layer_scales``)."""
+        if not self.fp8:
+            raise ValueError("scales apply to FP8 (e4m3) pools only")
+        self.k_scales.copy_(torch.as_tensor(k_scales, dtype=torch.float32))
+        self.v_scales.copy_(torch.as_tensor(v_scales, dtype=torch.float32))
+
+    def layer_scales(self, layer: int) -> tuple[torch.Tensor, torch.Tensor]:
+        """FP8 pools: (k_scale, v_scale) [n_kv_head] of one layer."""
+        return self.k_scales[layer], self.v_scales[layer]
 
     # -- block accounting --------------------------------------------------
     @property
@@ -212,4 +238,8 @@ class TorchBlockAllocator:
         n_layer = self.model_cfg.n_layer
         ks = [self.pool[layer, 0] for layer in range(n_layer)]
         vs = [self.pool[layer, 1] for layer in range(n_layer)]
-        ops.write_kv(ks, vs, ids, int(start), dev(k), dev(v))
+        if self.fp8:
+            ops.write_kv_scaled(ks, vs, ids, int(start), dev(k), dev(v), self.k_scales,
+                                self.v_scales)
+        else:
+            ops.write_kv(ks, vs, ids, int(start), dev(k), dev(v))

@@ -43,11 +43,14 @@ paged_attention_prefill_simt = _ext.paged_attention_prefill_simt
 write_kv = _ext.write_kv
 validate_block_tables = _ext.validate_block_tables
 merge_states = _ext.merge_states
+paged_attention_v3_fp8 = _ext.paged_attention_v3_fp8
+write_kv_scaled = _ext.write_kv_scaled
 
 __all__ = ["paged_attention", "paged_attention_v2", "paged_attention_v3",
            "paged_attention_v3_lse", "choose_num_splits", "paged_attention_prefill",
            "paged_attention_prefill_wmma", "paged_attention_prefill_simt", "write_kv",
-           "validate_block_tables", "merge_states", "shim_path"]
+           "validate_block_tables", "merge_states", "paged_attention_v3_fp8",
+           "write_kv_scaled", "shim_path"]
 
 
 def shim_path() -> Path:

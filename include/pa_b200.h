@@ -19,7 +19,8 @@
  *   q            [B, Sq, H, D]    fp32, contiguous  (prefill)
  *   k/v cache    [NB, BS, HKV, D] one layer's view pool[layer, 0|1] of the
  *                                 [n_layer, 2, NB, BS, HKV, D] pool, any of
- *                                 fp32 / fp16 / bf16 / fp64 (PA_DTYPE_*)
+ *                                 fp32 / fp16 / bf16 / fp64 (PA_DTYPE_*), or
+ *                                 fp8 e4m3 for decode
  *   block_tables [B, MB]          int32; token j of sequence b lives in block
  *                                 block_tables[b][j / BS], row j % BS
  *   context_lens [B]              int32
@@ -57,7 +58,12 @@ typedef enum pa_dtype {
   PA_DTYPE_F32 = 0,
   PA_DTYPE_F16 = 1,
   PA_DTYPE_BF16 = 2,
-  PA_DTYPE_F64 = 3
+  PA_DTYPE_F64 = 3,
+  /* OCP FP8 E4M3 ("e4m3fn": no infinities, max 448, 0x7f/0xff NaN), one
+   * byte per element, dequantised as value * scale with an fp32 scale per KV
+   * head (pa_paged_attention_v3_fp8, pa_write_kv_scaled; the entry points
+   * without scales use 1.0).  Decode and write_kv only. */
+  PA_DTYPE_E4M3 = 4
 } pa_dtype;
 
 /* host-side status codes (return values) */
@@ -179,6 +185,25 @@ PA_API int pa_paged_attention_v3_noalloc(
     int64_t num_kv_heads, int64_t head_dim, int64_t block_size,
     int64_t num_blocks, int64_t max_blocks, double scale, int64_t num_splits,
     int32_t* dev_status, void* stream);
+
+/* Decode of an FP8 (PA_DTYPE_E4M3) KV pool: an addition (the reference has
+ * fp32/fp16/fp64 pools only; FP8 KV is listed as not measured in its
+ * docs/REPORT.md:270).  Same arguments and results as pa_paged_attention_v3
+ * with the pool's elements dequantised as K = k_cache * k_scale[h],
+ * V = v_cache * v_scale[h]: k_scale / v_scale are device fp32 arrays of
+ * num_kv_heads entries (NULL = 1.0) for this layer.  kv_dtype must be
+ * PA_DTYPE_E4M3; the workspace is pa_decode_workspace_size's for that dtype. */
+PA_API int pa_paged_attention_v3_fp8(float* out, float* lse, const float* q,
+                                     const void* k_cache, const void* v_cache,
+                                     const float* k_scale, const float* v_scale,
+                                     int kv_dtype, const int32_t* block_tables,
+                                     const int32_t* context_lens, int64_t num_seqs,
+                                     int64_t num_heads, int64_t num_kv_heads,
+                                     int64_t head_dim, int64_t block_size,
+                                     int64_t num_blocks, int64_t max_blocks,
+                                     double scale, int64_t num_splits, void* workspace,
+                                     size_t workspace_bytes, int32_t* dev_status,
+                                     void* stream);
 
 /* Merge per-device partial results of one decode (sequence-sharded
  * long-context decode): out[b,h,:] = sum_r w_r out_r[b,h,:] / sum_r w_r with
@@ -310,6 +335,20 @@ PA_API int pa_write_kv(void* const* k_layers, void* const* v_layers, int pool_dt
                 int64_t num_layers, int64_t num_kv_heads, int64_t head_dim,
                 int64_t block_size, int64_t num_blocks, int32_t* dev_status,
                 void* stream);
+
+/* pa_write_kv with per-(layer, kv head) scales for an FP8 pool: element x is
+ * stored as e4m3(x / scale) (IEEE fp32 division, then round to nearest even,
+ * saturating to +-448; NaN stays NaN).  k_scales / v_scales: device fp32
+ * [num_layers, num_kv_heads] (NULL = 1.0); ignored for other pool dtypes. */
+PA_API int pa_write_kv_scaled(void* const* k_layers, void* const* v_layers, int pool_dtype,
+                              const void* k_src, const void* v_src, int src_dtype,
+                              int64_t src_layer_stride, int64_t src_head_stride,
+                              int64_t src_token_stride, const int32_t* block_ids,
+                              int64_t num_block_ids, int64_t start, int64_t num_tokens,
+                              int64_t num_layers, int64_t num_kv_heads, int64_t head_dim,
+                              int64_t block_size, int64_t num_blocks,
+                              const float* k_scales, const float* v_scales,
+                              int32_t* dev_status, void* stream);
 
 /* Opt-in check of a block table (the reference has none): counts entries
  * used by context_lens that fall outside [0, num_blocks), and sequences whose
