@@ -97,6 +97,7 @@ struct PlanParams {
   int32_t* dev_status;
   int64_t B, H, D, max_ctx, qlen;
   int32_t NGC, N;
+  int32_t tt;  // tokens per tile
   float empty_fill;
 };
 
@@ -130,7 +131,7 @@ __global__ void __launch_bounds__(kPlanThreads) plan_kernel(const __grid_constan
         if (pp.lse)
           for (int64_t h = 0; h < pp.H; ++h) pp.lse[b * pp.H + h] = -INFINITY;
       }
-      tiles = (int32_t)((n + kTT - 1) / kTT);
+      tiles = (int32_t)((n + pp.tt - 1) / pp.tt);
     }
     int32_t x = tiles;
 #pragma unroll
@@ -240,7 +241,7 @@ static int check_args(const DecodeArgs& a) {
   if (a.D != 32 && a.D != 64 && a.D != 128 && a.D != 256) return PA_ERR_HEAD_DIM;
   if (dtype_size(a.dtype) == 0) return PA_ERR_DTYPE;
   if (a.qlen < 1) return PA_ERR_INVALID_ARGUMENT;
-  if (a.B * a.qlen > (int64_t(1) << 30) || a.MB * a.BS > (int64_t(1) << 31) - kTT)
+  if (a.B * a.qlen > (int64_t(1) << 30) || a.MB * a.BS > (int64_t(1) << 31) - 2 * kTT)
     return PA_ERR_TOO_LARGE;
   return PA_OK;
 }
@@ -249,6 +250,7 @@ static int check_args(const DecodeArgs& a) {
 // layout.  Needs the current device (SM count, occupancy).
 static int configure(const DecodeArgs& a, Config* c) {
   const int elt = dtype_size(a.dtype);
+  const int tt = tile_tokens(a.dtype);
   const int QPK = (int)(a.H / a.HKV);
   const int epl = decode_elems_per_lane(a.dtype, (int)a.D);
   // Query heads per consumer warp: the largest group whose state fits (each
@@ -259,7 +261,7 @@ static int configure(const DecodeArgs& a, Config* c) {
     for (int g = (int)std::min<int64_t>(a.HKV, 64); g >= 1; --g) {
       if (a.HKV % g) continue;
       if (g * (QPK / qc) > maxw) continue;
-      if (2u * kTT * (uint32_t)(g * a.D * elt) > kStageCap) continue;
+      if (2u * tt * (uint32_t)(g * a.D * elt) > kStageCap) continue;
       return g;
     }
     return 0;
@@ -283,7 +285,7 @@ static int configure(const DecodeArgs& a, Config* c) {
   if (c->NS > maxw) return PA_ERR_TOO_LARGE;  // QPK / QC beyond one CTA
   c->NGC = (int)(a.HKV / G);
   c->row_bytes = (uint32_t)(G * a.D * elt);
-  const uint32_t stage_bytes = 2u * kTT * c->row_bytes;
+  const uint32_t stage_bytes = 2u * tt * c->row_bytes;
   c->nstage = (int)std::max<uint32_t>(2, std::min<uint32_t>(8, kRingBudget / stage_bytes));
   // must match decode::Limits
   {
@@ -295,7 +297,7 @@ static int configure(const DecodeArgs& a, Config* c) {
   if (!c->kernel) return PA_ERR_HEAD_DIM;
 
   const int64_t rows = a.B * a.qlen;
-  const int64_t max_tiles = (a.MB * a.BS + kTT - 1) / kTT;
+  const int64_t max_tiles = (a.MB * a.BS + tt - 1) / tt;
   const int64_t t_upper = std::max<int64_t>(1, (int64_t)c->NGC * rows * max_tiles);
   int64_t N;
   if (a.num_splits <= 0) {
@@ -368,6 +370,7 @@ int launch(const DecodeArgs& a, void* ws, size_t ws_bytes, cudaStream_t stream) 
   pp.NGC = c.NGC;
   pp.N = c.N;
   pp.empty_fill = a.empty_fill;
+  pp.tt = tile_tokens(a.dtype);
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = 1;
@@ -399,7 +402,8 @@ int launch(const DecodeArgs& a, void* ws, size_t ws_bytes, cudaStream_t stream) 
   p.abort_flag = reinterpret_cast<int32_t*>(w + c.off_abort);
   next_epoch(&p.epoch, &p.abort_tag);
   p.empty_fill = a.empty_fill;
-  p.beta = c.fused ? kStartTiles : 0;
+  // the start cost is in 16-token tiles: fewer of the larger FP8 tiles
+  p.beta = c.fused ? kStartTiles * kTT / tile_tokens(a.dtype) : 0;
   p.partials = reinterpret_cast<float*>(w + c.off_part);
   p.B = a.B * a.qlen;
   p.qlen = a.qlen;

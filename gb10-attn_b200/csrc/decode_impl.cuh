@@ -6,7 +6,7 @@
 // context, un-normalised partials, log-sum-exp merge (:113-122, :139-165).
 // Different machine mapping:
 //
-//   * Work unit = a tile of kTT = 16 consecutive tokens of one sequence for a
+//   * Work unit = a tile of kTT = 16 (FP8 pools: 32) consecutive tokens of one sequence for a
 //     group of G kv heads ("g-chunk").  The NGC * sum_b ceil(ctx_b / 16) tiles
 //     are split into N contiguous ranges, one per CTA (N = SMs x resident CTAs
 //     for automatic splitting), so every SM streams about the same number of
@@ -40,12 +40,20 @@
 namespace pa {
 namespace decode {
 
-constexpr int kTT = 16;            // tokens per pipeline stage
+constexpr int kTT = 16;            // tokens per pipeline stage (16-bit and wider pools)
 constexpr int kGroup = 8;          // pieces merged per step of a split sequence
 constexpr int kFusedRows = 1024;   // rows up to which each CTA plans for itself
 constexpr int kCountBits = 24;     // arrival count bits of an epoch-tagged counter
 constexpr int kPlanScratchBytes = 272;  // scan scratch ahead of the fused plan tables
 constexpr float kNegBig = -3.0e38f;  // the reference's "minus infinity" (paged_attn_v3.cu:20)
+
+// FP8 pools use 32-token stages: the bytes of a 16-bit pool's 16 tokens, and
+// twice the rows per consumer lane for each stage wait.
+template <typename T>
+struct Tile {
+  static constexpr int TT = sizeof(T) == 1 ? 2 * kTT : kTT;
+};
+inline int tile_tokens(int dtype) { return dtype_size(dtype) == 1 ? 2 * kTT : kTT; }
 
 struct Params {
   float* out;                    // [B, H, D]
@@ -107,8 +115,8 @@ struct Geo {
   static constexpr int NCH = CH / R;                      // chunks per lane
   static constexpr int EPL = NCH * VEC;                   // elements per lane
   static constexpr int NRG = 32 / R;                      // row groups per warp
-  static constexpr int TPR = kTT / NRG;                   // tokens per row group per stage
-  static_assert(D % VEC == 0 && CH % R == 0 && 32 % R == 0 && NRG <= kTT, "geometry");
+  static constexpr int TPR = Tile<T>::TT / NRG;          // tokens per row group per stage
+  static_assert(D % VEC == 0 && CH % R == 0 && 32 % R == 0 && NRG <= Tile<T>::TT, "geometry");
 };
 
 // CTA shape of a (T, D, QC) instantiation, by the per-lane register state
@@ -173,7 +181,7 @@ __device__ __forceinline__ int epoch_arrive(unsigned long long* counter, unsigne
 // (the plan kernel's rule: a query row s of qlen sees context - qlen + s + 1
 // keys, clamped to the block table).  CTA b % gridDim fills the output rows of
 // empty sequences (the reference's v3 yields NaN there, paged_attn_v3.cu:160-165).
-template <int D>
+template <int D, int TT>
 __device__ __forceinline__ void fused_plan(const Params& p, int32_t* tile_off_s, int32_t* ntok_s,
                                            int32_t* ne_s, long long* scratch) {
   // one scan carries both counts: tiles in the high bits, non-empty rows in
@@ -202,7 +210,7 @@ __device__ __forceinline__ void fused_plan(const Params& p, int32_t* tile_off_s,
         }
       }
       ntok_s[b] = (int32_t)n;
-      tiles = (int32_t)((n + kTT - 1) / kTT);
+      tiles = (int32_t)((n + TT - 1) / TT);
     }
     const long long mine = ((long long)tiles << 16) | (tiles > 0 ? 1 : 0);
     long long x = mine;
@@ -354,7 +362,8 @@ __global__ void __launch_bounds__(Limits<T, D, QC>::THREADS, 1)
 
   extern __shared__ __align__(128) unsigned char smem[];
   const int nstage = p.nstage;
-  const uint32_t stage_bytes = 2u * kTT * p.row_bytes;
+  constexpr int TT = Tile<T>::TT;
+  const uint32_t stage_bytes = 2u * TT * p.row_bytes;
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + (size_t)nstage * stage_bytes);
   uint64_t* empty = full + nstage;
   StageHeader* hdr = reinterpret_cast<StageHeader*>(empty + nstage);
@@ -389,7 +398,7 @@ __global__ void __launch_bounds__(Limits<T, D, QC>::THREADS, 1)
     int32_t* to_s = reinterpret_cast<int32_t*>(plan_base + kPlanScratchBytes);
     int32_t* nt_s = to_s + p.B + 1;
     int32_t* nz_s = nt_s + p.B;
-    fused_plan<D>(p, to_s, nt_s, nz_s, reinterpret_cast<long long*>(plan_base));
+    fused_plan<D, Tile<T>::TT>(p, to_s, nt_s, nz_s, reinterpret_cast<long long*>(plan_base));
     tile_off = to_s;
     ntok_s = nt_s;
     ne_s = nz_s;
@@ -512,8 +521,8 @@ __global__ void __launch_bounds__(Limits<T, D, QC>::THREADS, 1)
 
       while (gt < hi) {
         const int64_t t_in_seq = r - s0;
-        const int64_t tok0 = t_in_seq * kTT;
-        const int nvalid = (int)(n_tok - tok0 < kTT ? n_tok - tok0 : kTT);
+        const int64_t tok0 = t_in_seq * TT;
+        const int nvalid = (int)(n_tok - tok0 < TT ? n_tok - tok0 : TT);
         // block-table window: lane l holds bt[win_base + l] (cur) and
         // bt[win_base + 32 + l] (next); `next` is loaded a window ahead.
         const int64_t pg_lo = tok0 / p.BS;
@@ -529,15 +538,22 @@ __global__ void __launch_bounds__(Limits<T, D, QC>::THREADS, 1)
         }
         if (!mbar_wait(&empty[stage], phase ^ 1, p.abort_flag, p.abort_tag)) { ok = false; break; }
 
-        const int row = lane & 15, kv = lane >> 4;
-        const int64_t tok = tok0 + row;
-        const int64_t pg = tok / p.BS;
-        const int idx = (int)(pg - win_base);
-        const int32_t a = __shfl_sync(0xffffffffu, win_cur, idx & 31);
-        const int32_t c = __shfl_sync(0xffffffffu, win_next, idx & 31);
-        int64_t blk = idx < 32 ? a : c;
+        // lane = (row % 16, K|V); TT / 16 rows per lane
+        constexpr int RPL = TT / 16;
+        const int kv = lane >> 4;
+        int64_t blk_r[RPL], pg_r[RPL];
         bool bad = false;
-        if (row < nvalid && (blk < 0 || blk >= p.NB)) { bad = true; blk = 0; }
+#pragma unroll
+        for (int hh = 0; hh < RPL; ++hh) {
+          const int row = (lane & 15) + 16 * hh;
+          const int64_t pg = (tok0 + row) / p.BS;
+          pg_r[hh] = pg;
+          const int idx = (int)(pg - win_base);
+          const int32_t a = __shfl_sync(0xffffffffu, win_cur, idx & 31);
+          const int32_t c = __shfl_sync(0xffffffffu, win_next, idx & 31);
+          blk_r[hh] = idx < 32 ? a : c;
+          if (row < nvalid && (blk_r[hh] < 0 || blk_r[hh] >= p.NB)) { bad = true; blk_r[hh] = 0; }
+        }
         if (__any_sync(0xffffffffu, bad) && lane == 0) report(p.dev_status, PA_DEVERR_BLOCK_ID);
 
         if (lane == 0) {
@@ -558,17 +574,20 @@ __global__ void __launch_bounds__(Limits<T, D, QC>::THREADS, 1)
           mbar_arrive_expect_tx(&full[stage], (uint32_t)nvalid * 2u * p.row_bytes);
         }
         __syncwarp();
-        if (row < nvalid) {
-          const int64_t off = tok - pg * p.BS;
-          const char* src = (kv ? p.v_cache : p.k_cache) + blk * p.blk_stride +
+#pragma unroll
+        for (int hh = 0; hh < RPL; ++hh) {
+          const int row = (lane & 15) + 16 * hh;
+          if (row >= nvalid) continue;
+          const int64_t off = tok0 + row - pg_r[hh] * p.BS;
+          const char* src = (kv ? p.v_cache : p.k_cache) + blk_r[hh] * p.blk_stride +
                             off * p.tok_stride + (int64_t)gc * gbytes;
           unsigned char* dst = smem + (size_t)stage * stage_bytes +
-                               (size_t)(kv * kTT + row) * p.row_bytes;
+                               (size_t)(kv * TT + row) * p.row_bytes;
           if (p.rows_contiguous) {
             // The g-chunk spans every KV head, so the tile's rows that share a
             // page are one contiguous run of bytes: one bulk copy per run,
             // issued by the run's first row (one K + one V copy per tile when
-            // 16 | block_size).
+            // the tile size divides block_size).
             if (row == 0 || off == 0) {
               const int64_t run = min((int64_t)(nvalid - row), p.BS - off);
               bulk_g2s(dst, src, (uint32_t)run * p.row_bytes, &full[stage]);
@@ -771,7 +790,7 @@ __global__ void __launch_bounds__(Limits<T, D, QC>::THREADS, 1)
 
     const unsigned char* kbase =
         smem + (size_t)stage * stage_bytes + (size_t)g_local * D * sizeof(T);
-    const unsigned char* vbase = kbase + (size_t)kTT * p.row_bytes;
+    const unsigned char* vbase = kbase + (size_t)TT * p.row_bytes;
     const int nvalid = h.nvalid;
 
     // scores of this row group's tokens for the QC heads (packed pairs:

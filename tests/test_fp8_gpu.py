@@ -87,6 +87,8 @@ def oracle_lse(q, k, bt, ctx, scale):
     (2, 8, 2, 32, 16, [700, 1500]),
     (2, 4, 4, 256, 16, [900, 64]),
     (3, 16, 4, 128, 8, [333, 1200, 17]),    # block size 8
+    (2, 8, 8, 64, 48, [1000, 77]),          # 32-token tiles straddle 48-token pages
+    (2, 4, 4, 64, 1, [200, 33]),            # one token per page
 ])
 def test_decode_matches_oracle(B, H, HKV, D, BS, ctx):
     q, kd, vd, bt, ctxs, dev = fp8_case(70 + D, B, H, HKV, D, BS, ctx)
