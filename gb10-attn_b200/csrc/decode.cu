@@ -425,6 +425,10 @@ int launch(const DecodeArgs& a, void* ws, size_t ws_bytes, cudaStream_t stream) 
   p.rows_contiguous = (c.G == a.HKV) ? 1 : 0;
   const int elt = dtype_size(a.dtype);
   p.tok_stride = a.HKV * a.D * elt;
+  p.bs_shift = -1;
+  if ((a.BS & (a.BS - 1)) == 0)
+    for (int sh = 0; sh < 32; ++sh)
+      if ((int64_t(1) << sh) == a.BS) p.bs_shift = sh;
   p.blk_stride = a.BS * p.tok_stride;
 
   cudaLaunchConfig_t cfg = {};

@@ -96,6 +96,7 @@ struct Params {
   uint32_t row_bytes;            // G * D * sizeof(T)
   int32_t rows_contiguous;       // G == HKV: a page's token rows are adjacent
   int64_t tok_stride;            // HKV * D * sizeof(T): one token row of a page
+  int32_t bs_shift;              // log2(BS) when BS is a power of two, else -1
   int64_t blk_stride;            // BS * tok_stride: one page
 };
 
@@ -525,7 +526,13 @@ __global__ void __launch_bounds__(Limits<T, D, QC>::THREADS, 1)
         const int nvalid = (int)(n_tok - tok0 < TT ? n_tok - tok0 : TT);
         // block-table window: lane l holds bt[win_base + l] (cur) and
         // bt[win_base + 32 + l] (next); `next` is loaded a window ahead.
-        const int64_t pg_lo = tok0 / p.BS;
+        // page of a token: a shift, or a 32-bit division (every token index
+        // is below 2^31, MB * BS being checked on the host)
+        auto page_of = [&](int64_t tok) -> int64_t {
+          return p.bs_shift >= 0 ? (tok >> p.bs_shift)
+                                 : (int64_t)((uint32_t)tok / (uint32_t)p.BS);
+        };
+        const int64_t pg_lo = page_of(tok0);
         if (win_base < 0 || pg_lo >= win_base + 32) {
           if (win_base >= 0 && pg_lo < win_base + 64) {
             win_base += 32;
@@ -546,7 +553,7 @@ __global__ void __launch_bounds__(Limits<T, D, QC>::THREADS, 1)
 #pragma unroll
         for (int hh = 0; hh < RPL; ++hh) {
           const int row = (lane & 15) + 16 * hh;
-          const int64_t pg = (tok0 + row) / p.BS;
+          const int64_t pg = page_of(tok0 + row);
           pg_r[hh] = pg;
           const int idx = (int)(pg - win_base);
           const int32_t a = __shfl_sync(0xffffffffu, win_cur, idx & 31);
