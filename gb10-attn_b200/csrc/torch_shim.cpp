@@ -367,6 +367,65 @@ void write_kv_scaled(std::vector<torch::Tensor> k_layers, std::vector<torch::Ten
                 v_scales, "write_kv_scaled");
 }
 
+// One decode step's append: k_new / v_new [n_layer, B, HKV, D] go to position
+// positions[b] (< 0: skipped) of sequence b through its block-table row.
+// k_scales / v_scales: FP8 pools only ([n_layer, HKV], may be empty tensors).
+void append_kv(std::vector<torch::Tensor> k_layers, std::vector<torch::Tensor> v_layers,
+               torch::Tensor block_tables, torch::Tensor positions, torch::Tensor k_new,
+               torch::Tensor v_new, torch::Tensor k_scales, torch::Tensor v_scales) {
+  const char* op = "append_kv";
+  TORCH_CHECK(!k_layers.empty() && k_layers.size() == v_layers.size(),
+              op, ": need one K and one V tensor per layer");
+  const torch::Tensor& k0 = k_layers[0];
+  TORCH_CHECK(k0.is_cuda() && k0.dim() == 4, op, ": pool tensors must be CUDA [NB, BS, H, D]");
+  const int64_t L = (int64_t)k_layers.size();
+  TORCH_CHECK(k_new.dim() == 4 && v_new.sizes() == k_new.sizes() && k_new.size(0) == L &&
+                  k_new.size(2) == k0.size(2) && k_new.size(3) == k0.size(3),
+              op, ": k_new, v_new must be [n_layer, B, HKV, D]");
+  const c10::cuda::CUDAGuard guard(k0.device());
+  std::vector<void*> kp, vp;
+  const int pdt = pool_dtype(k0, op);
+  for (int64_t l = 0; l < L; ++l) {
+    for (const torch::Tensor* t : {&k_layers[l], &v_layers[l]}) {
+      TORCH_CHECK(t->is_contiguous() && t->sizes() == k0.sizes() &&
+                      t->scalar_type() == k0.scalar_type() && t->device() == k0.device(),
+                  op, ": pool tensors must be contiguous and alike");
+    }
+    kp.push_back(k_layers[l].data_ptr());
+    vp.push_back(v_layers[l].data_ptr());
+  }
+  torch::Tensor kd = k_new.to(k0.device());
+  torch::Tensor vd = v_new.to(k0.device());
+  int sdt;
+  switch (kd.scalar_type()) {
+    case torch::kFloat: sdt = PA_DTYPE_F32; break;
+    case torch::kHalf: sdt = PA_DTYPE_F16; break;
+    case torch::kBFloat16: sdt = PA_DTYPE_BF16; break;
+    default:
+      kd = kd.to(torch::kFloat);
+      sdt = PA_DTYPE_F32;
+  }
+  kd = kd.contiguous();
+  vd = vd.to(kd.scalar_type()).contiguous();
+  torch::Tensor bt = block_tables.to(k0.device(), torch::kInt32).contiguous();
+  torch::Tensor pos = positions.to(k0.device(), torch::kInt32).contiguous();
+  const int64_t B = kd.size(1);
+  TORCH_CHECK(bt.dim() == 2 && bt.size(0) >= B && pos.numel() >= B,
+              op, ": block_tables [B, MB] and positions [B] needed");
+  torch::Tensor ks, vs;
+  if (k_scales.defined() && k_scales.numel()) ks = k_scales.to(k0.device(), torch::kFloat).contiguous();
+  if (v_scales.defined() && v_scales.numel()) vs = v_scales.to(k0.device(), torch::kFloat).contiguous();
+  for (const torch::Tensor* t : {&ks, &vs})
+    TORCH_CHECK(!t->defined() || t->numel() == L * k0.size(2), op, ": scales must be [n_layer, HKV]");
+  check_status(pa_append_kv(kp.data(), vp.data(), pdt, kd.data_ptr(), vd.data_ptr(), sdt,
+                            bt.data_ptr<int32_t>(), bt.size(1), pos.data_ptr<int32_t>(), B, L,
+                            k0.size(2), k0.size(3), k0.size(1), k0.size(0),
+                            ks.defined() ? ks.data_ptr<float>() : nullptr,
+                            vs.defined() ? vs.data_ptr<float>() : nullptr, nullptr,
+                            stream_ptr()),
+               op);
+}
+
 // Counts of (out-of-range block ids, over-long contexts); synchronises.
 std::tuple<int64_t, int64_t> validate_block_tables(torch::Tensor block_tables,
                                                    torch::Tensor context_lens,
@@ -413,6 +472,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("paged_attention_prefill_simt", &paged_attention_prefill_simt);
   m.def("write_kv", &write_kv);
   m.def("write_kv_scaled", &write_kv_scaled);
+  m.def("append_kv", &append_kv);
   m.def("paged_attention_v3_fp8", &paged_attention_v3_fp8);
   m.def("validate_block_tables", &validate_block_tables);
   m.def("merge_states", &merge_states);

@@ -1,4 +1,5 @@
-// write_kv.cu -- KV-pool writer (C ABI pa_write_kv, pa_write_kv_scaled).
+// write_kv.cu -- KV-pool writer (C ABI pa_write_kv, pa_write_kv_scaled) and the
+// batched one-token append of a decode step (pa_append_kv).
 //
 // Replaces hetero-serve TorchBlockAllocator.write_kv(block_ids, start, k, v)
 // (heteroserve/kv/torch_blocks.py:92, un-vendored; behaviour from the call
@@ -34,6 +35,10 @@ struct Params {
   const int32_t* block_ids;
   int64_t n_ids;
   int64_t start, T, L, HKV, D, BS, NB;
+  // Batched append (pa_append_kv): source token t is the next token of
+  // sequence t, at position positions[t] (< 0: none), and block_ids is the
+  // [T, n_ids] block table.  Null for the one-sequence writer.
+  const int32_t* positions;
   // FP8 pools: [L, HKV] quantisation scales (null = 1); this launch's layers
   const float* k_scales;
   const float* v_scales;
@@ -82,13 +87,25 @@ __global__ void __launch_bounds__(256) write_kv_kernel(const __grid_constant__ P
     const int kv = (int)(row % 2);
     const int64_t l = row / 2;
 
-    const int64_t pos = p.start + t;
-    const int64_t page = pos / p.BS;
-    if (page >= p.n_ids) {
-      if (chunk == 0) report(p.dev_status, PA_DEVERR_BLOCK_ID);
-      continue;
+    int64_t pos, page, blk;
+    if (p.positions) {
+      pos = p.positions[t];
+      if (pos < 0) continue;
+      page = pos / p.BS;
+      if (page >= p.n_ids) {  // past the sequence's block table
+        if (chunk == 0) report(p.dev_status, PA_DEVERR_CONTEXT);
+        continue;
+      }
+      blk = p.block_ids[t * p.n_ids + page];
+    } else {
+      pos = p.start + t;
+      page = pos / p.BS;
+      if (page >= p.n_ids) {
+        if (chunk == 0) report(p.dev_status, PA_DEVERR_BLOCK_ID);
+        continue;
+      }
+      blk = p.block_ids[page];
     }
-    const int64_t blk = p.block_ids[page];
     if (blk < 0 || blk >= p.NB) {
       if (chunk == 0) report(p.dev_status, PA_DEVERR_BLOCK_ID);
       continue;
@@ -231,6 +248,68 @@ extern "C" int pa_write_kv_scaled(void* const* k_layers, void* const* v_layers, 
     p.n_ids = num_block_ids;
     p.start = start;
     p.T = num_tokens;
+    p.L = nl;
+    p.HKV = num_kv_heads;
+    p.D = head_dim;
+    p.BS = block_size;
+    p.NB = num_blocks;
+    p.k_scales = k_scales ? k_scales + l0 * num_kv_heads : nullptr;
+    p.v_scales = v_scales ? v_scales + l0 * num_kv_heads : nullptr;
+    p.dev_status = dev_status;
+    int st;
+    switch (src_dtype) {
+      case PA_DTYPE_F32: st = writekv::launch_src<float>(p, pool_dtype, vec, s); break;
+      case PA_DTYPE_F16: st = writekv::launch_src<__half>(p, pool_dtype, vec, s); break;
+      default: st = writekv::launch_src<__nv_bfloat16>(p, pool_dtype, vec, s); break;
+    }
+    if (st) return st;
+  }
+  return PA_OK;
+}
+
+extern "C" int pa_append_kv(void* const* k_layers, void* const* v_layers, int pool_dtype,
+                            const void* k_new, const void* v_new, int src_dtype,
+                            const int32_t* block_tables, int64_t max_blocks,
+                            const int32_t* positions, int64_t num_seqs, int64_t num_layers,
+                            int64_t num_kv_heads, int64_t head_dim, int64_t block_size,
+                            int64_t num_blocks, const float* k_scales, const float* v_scales,
+                            int32_t* dev_status, void* stream) {
+  using namespace pa;
+  using writekv::kMaxLayers;
+  if (num_seqs < 0 || num_layers < 0 || num_kv_heads <= 0 || head_dim <= 0 ||
+      block_size <= 0 || num_blocks < 0 || max_blocks < 0)
+    return PA_ERR_INVALID_ARGUMENT;
+  if (num_seqs == 0 || num_layers == 0) return PA_OK;
+  if (!k_layers || !v_layers || !k_new || !v_new || !block_tables || !positions)
+    return PA_ERR_INVALID_ARGUMENT;
+  if (src_dtype != PA_DTYPE_F32 && src_dtype != PA_DTYPE_F16 && src_dtype != PA_DTYPE_BF16)
+    return PA_ERR_DTYPE;
+  const int ps = dtype_size(pool_dtype), ss = dtype_size(src_dtype);
+  if (ps == 0) return PA_ERR_DTYPE;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  // source [num_layers, num_seqs, num_kv_heads, head_dim], contiguous
+  const int64_t head_stride = head_dim, seq_stride = num_kv_heads * head_dim;
+  const int64_t layer_stride = num_seqs * seq_stride;
+  for (int64_t l0 = 0; l0 < num_layers; l0 += kMaxLayers) {
+    const int64_t nl = std::min<int64_t>(kMaxLayers, num_layers - l0);
+    writekv::Params p = {};
+    bool vec = (head_dim % 8 == 0) && aligned16(k_new) && aligned16(v_new) &&
+               (head_dim * ss) % 16 == 0 && (head_dim * ps) % 16 == 0;
+    for (int64_t l = 0; l < nl; ++l) {
+      p.k_layers[l] = static_cast<char*>(k_layers[l0 + l]);
+      p.v_layers[l] = static_cast<char*>(v_layers[l0 + l]);
+      if (!p.k_layers[l] || !p.v_layers[l]) return PA_ERR_INVALID_ARGUMENT;
+      vec = vec && aligned16(p.k_layers[l]) && aligned16(p.v_layers[l]);
+    }
+    p.k_src = static_cast<const char*>(k_new) + l0 * layer_stride * ss;
+    p.v_src = static_cast<const char*>(v_new) + l0 * layer_stride * ss;
+    p.src_layer_stride = layer_stride;
+    p.src_head_stride = head_stride;
+    p.src_token_stride = seq_stride;
+    p.block_ids = block_tables;
+    p.n_ids = max_blocks;
+    p.positions = positions;
+    p.T = num_seqs;
     p.L = nl;
     p.HKV = num_kv_heads;
     p.D = head_dim;

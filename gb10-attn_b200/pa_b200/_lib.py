@@ -74,6 +74,8 @@ SIGNATURES = {
                     [_P, _P]),
     "pa_write_kv_scaled": (_I, [_P, _P, _I, _P, _P, _I, _I64, _I64, _I64, _P] + [_I64] * 8 +
                            [_P, _P, _P, _P]),
+    "pa_append_kv": (_I, [_P, _P, _I, _P, _P, _I, _P, _I64, _P] + [_I64] * 6 +
+                     [_P, _P, _P, _P]),
     "pa_validate_block_tables": (_I, [_P, _P, _I64, _I64, _I64, _I64, _P, _P]),
 }
 

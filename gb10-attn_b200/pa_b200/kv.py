@@ -214,6 +214,23 @@ class TorchBlockAllocator:
             bt[i, :len(a.block_ids)] = torch.tensor(a.block_ids, dtype=torch.int32)
         return bt.to(self.device)
 
+    # -- decode-step append -----------------------------------------------------
+    def append_kv(self, block_tables, positions, k_new, v_new) -> None:
+        """Write one new token per sequence for every layer (a decode step).
+
+        k_new, v_new: [n_layer, B, n_kv_head, head_dim] (any device; fp32 /
+        fp16 / bf16); sequence b's token lands at position positions[b]
+        (< 0: none) through row b of block_tables."""
+        from . import ops
+        n_layer = self.model_cfg.n_layer
+        ks = [self.pool[layer, 0] for layer in range(n_layer)]
+        vs = [self.pool[layer, 1] for layer in range(n_layer)]
+        empty = torch.empty(0)
+        ops.append_kv(ks, vs, torch.as_tensor(block_tables), torch.as_tensor(positions),
+                      torch.as_tensor(k_new), torch.as_tensor(v_new),
+                      self.k_scales if self.fp8 else empty,
+                      self.v_scales if self.fp8 else empty)
+
     # -- writer ----------------------------------------------------------------
     def write_kv(self, block_ids, start: int, k, v) -> None:
         """Write K/V of one sequence for every layer.

@@ -350,6 +350,25 @@ PA_API int pa_write_kv_scaled(void* const* k_layers, void* const* v_layers, int 
                               const float* k_scales, const float* v_scales,
                               int32_t* dev_status, void* stream);
 
+/* One decode step's K/V append for a batch, an addition (the reference
+ * writes whole sequences with write_kv only): for every layer l < num_layers,
+ * sequence b < num_seqs with positions[b] >= 0 and kv head h,
+ *   K_l[block_tables[b][p / BS], p % BS, h, :] = convert(k_new[l, b, h, :])
+ * (and V likewise) with p = positions[b], the slot of the sequence's next
+ * token.  k_new / v_new: device [num_layers, num_seqs, num_kv_heads,
+ * head_dim], contiguous, of src_dtype; block_tables: device int32
+ * [num_seqs, max_blocks]; positions: device int32 [num_seqs] (< 0 skips the
+ * sequence).  Conversion and FP8 scales as pa_write_kv_scaled (scales
+ * nullable).  A position past the block table is skipped and reported as
+ * PA_DEVERR_CONTEXT, a block id outside [0, num_blocks) as PA_DEVERR_BLOCK_ID. */
+PA_API int pa_append_kv(void* const* k_layers, void* const* v_layers, int pool_dtype,
+                        const void* k_new, const void* v_new, int src_dtype,
+                        const int32_t* block_tables, int64_t max_blocks,
+                        const int32_t* positions, int64_t num_seqs, int64_t num_layers,
+                        int64_t num_kv_heads, int64_t head_dim, int64_t block_size,
+                        int64_t num_blocks, const float* k_scales, const float* v_scales,
+                        int32_t* dev_status, void* stream);
+
 /* Opt-in check of a block table (the reference has none): counts entries
  * used by context_lens that fall outside [0, num_blocks), and sequences whose
  * context exceeds max_blocks * block_size.  Writes the two counts to the
