@@ -54,7 +54,9 @@ OCCUPANCY = "sm__warps_active.avg.pct_of_peak_sustained_active"
 L2_HIT = "lts__t_sector_hit_rate.pct"
 
 _BYTES = {"byte": 1, "kbyte": 1e3, "mbyte": 1e6, "gbyte": 1e9, "tbyte": 1e12}
-_TIME_NS = {"nsecond": 1, "usecond": 1e3, "msecond": 1e6, "second": 1e9}
+# the long form spells units out ("usecond"), the raw page abbreviates ("us")
+_TIME_NS = {"nsecond": 1, "usecond": 1e3, "msecond": 1e6, "second": 1e9,
+            "ns": 1, "us": 1e3, "ms": 1e6, "s": 1e9}
 
 
 def _number(text: str) -> float | None:

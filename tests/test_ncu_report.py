@@ -30,7 +30,7 @@ WIDE = "\n".join([
     '"ID","Process ID","Kernel Name","gpu__time_duration.sum","dram__bytes_read.sum",'
     '"dram__bytes_write.sum","dram__throughput.avg.pct_of_peak_sustained_elapsed",'
     '"sm__warps_active.avg.pct_of_peak_sustained_active","lts__t_sector_hit_rate.pct"',
-    '"","","","msecond","Gbyte","Mbyte","%","%","%"',
+    '"","","","ms","Gbyte","Mbyte","%","%","%"',
     '"0","9","prefill_tc_kernel<__nv_bfloat16, 128>","1.550","0.538","241.9","30.5","45.0","78.4"',
     '"1","9","prefill_tc_kernel<__nv_bfloat16, 128>","1.450","0.538","241.9","32.5","45.0","78.4"',
 ]) + "\n"
