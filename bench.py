@@ -460,54 +460,61 @@ def correctness_gate(torch, layer_call, pool, q, bt_np, bt_dev, ctx_dev, scale, 
 def run_e2e(torch, dist, args, layer_call, q_dev, tables, ctx_np, dev, stream, world, L,
             REGIONS):
     """Same decode steps through the public API with host buffers, as a serving
-    loop runs them: every step copies its q (all layers) and block table from
-    pinned host memory to the device and reads every layer's output back to
-    pinned host memory, all inside the timed region.  The copies go on a side
-    stream: layer l+1's q slice travels while layer l computes, and layer l's
-    output is read back while layer l+1 computes; the step's block table and
-    context lengths, and layer 0's q, are copied before its first kernel."""
+    loop runs them: every step copies its q (all layers), block table and
+    context lengths from pinned host memory to the device and reads every
+    layer's output back to pinned host memory, all inside the timed region.
+    The copies go on a side stream, pipelined by one step: step i+1's inputs
+    travel (into the other of two device input slots) while step i computes,
+    and step i's outputs are read back once its last layer is done.  A step's
+    12 layer kernels follow each other with no event between them, so each
+    launch overlaps the previous one's tail (programmatic dependent launch)."""
     q_host = torch.empty(tuple(q_dev.shape), dtype=torch.float32).pin_memory()
     q_host.copy_(q_dev.cpu())
     bt_host = [torch.from_numpy(t).pin_memory() for t in tables]
     ctx_host = torch.from_numpy(ctx_np).pin_memory()
     out_host = torch.empty(tuple(q_dev.shape), dtype=torch.float32).pin_memory()
-    qd = torch.empty_like(q_dev)
-    btd = torch.empty(tuple(tables[0].shape), dtype=torch.int32, device=dev)
-    cd = torch.empty(len(ctx_np), dtype=torch.int32, device=dev)
+    qd = [torch.empty_like(q_dev) for _ in range(2)]
+    btd = [torch.empty(tuple(tables[0].shape), dtype=torch.int32, device=dev) for _ in range(2)]
+    cd = [torch.empty(len(ctx_np), dtype=torch.int32, device=dev) for _ in range(2)]
     copy = torch.cuda.Stream(device=dev)
-    ev_in = [torch.cuda.Event() for _ in range(L)]
-    ev_out = [torch.cuda.Event() for _ in range(L)]
-    d2h_done = torch.cuda.Event()
-    held = []  # this step's outputs, alive until their read-back is done
+    ev_in = [torch.cuda.Event() for _ in range(2)]
+    ev_step = [torch.cuda.Event() for _ in range(2)]
+    d2h_done = [torch.cuda.Event() for _ in range(2)]
+    held = [[], []]  # each slot's outputs, alive until their read-back is done
 
-    def e2e_step(i: int):
-        # the previous step's outputs are released once the compute stream has
-        # waited for their read-back (stream-ordered reuse, no allocator sync)
-        stream.wait_event(d2h_done)
-        held.clear()
-        # inputs of this step: the device buffers are free once the previous
-        # step's last output was read back (the copy stream is in order)
+    def upload(i: int):
+        """Step i's inputs into slot i % 2, on the copy stream."""
+        s = i % 2
         with torch.cuda.stream(copy):
-            btd.copy_(bt_host[i % REGIONS], non_blocking=True)
-            cd.copy_(ctx_host, non_blocking=True)
-            qd[0].copy_(q_host[0], non_blocking=True)
-            ev_in[0].record(copy)
-        for layer in range(L):
-            if layer + 1 < L:
-                with torch.cuda.stream(copy):
-                    qd[layer + 1].copy_(q_host[layer + 1], non_blocking=True)
-                    ev_in[layer + 1].record(copy)
-            stream.wait_event(ev_in[layer])
-            out = layer_call(layer, qd[layer], btd, cd)
-            held.append(out)
-            ev_out[layer].record(stream)
-            with torch.cuda.stream(copy):
-                copy.wait_event(ev_out[layer])
-                out_host[layer].copy_(out, non_blocking=True)
-        d2h_done.record(copy)
+            btd[s].copy_(bt_host[i % REGIONS], non_blocking=True)
+            cd[s].copy_(ctx_host, non_blocking=True)
+            qd[s].copy_(q_host, non_blocking=True)
+            ev_in[s].record(copy)
 
-    for i in range(max(2, args.warmup)):
-        e2e_step(i)
+    def e2e_step(i: int, last: bool):
+        s = i % 2
+        # step i-2's outputs are released once the compute stream has waited
+        # for their read-back (stream-ordered reuse, no allocator sync)
+        stream.wait_event(d2h_done[s])
+        held[s].clear()
+        stream.wait_event(ev_in[s])
+        if not last:
+            # the other slot is free once step i-1's kernels are done with it
+            copy.wait_event(ev_step[1 - s])
+            upload(i + 1)
+        for layer in range(L):
+            held[s].append(layer_call(layer, qd[s][layer], btd[s], cd[s]))
+        ev_step[s].record(stream)
+        with torch.cuda.stream(copy):
+            copy.wait_event(ev_step[s])
+            for layer in range(L):
+                out_host[layer].copy_(held[s][layer], non_blocking=True)
+            d2h_done[s].record(copy)
+
+    n_warm = max(2, args.warmup)
+    upload(0)
+    for i in range(n_warm):
+        e2e_step(i, i + 1 == n_warm)
     torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
@@ -515,14 +522,16 @@ def run_e2e(torch, dist, args, layer_call, q_dev, tables, ctx_np, dev, stream, w
     done = torch.cuda.Event()
     e0.record(stream)
     copy.wait_event(e0)  # no copy of the timed steps starts before e0
+    upload(0)
     for i in range(args.steps):
-        e2e_step(i)
+        e2e_step(i, i + 1 == args.steps)
     done.record(copy)
     stream.wait_event(done)  # the last read-back is inside the timed region
     e1.record(stream)
     torch.cuda.synchronize()
-    # the overlapped loop must read back what a plain call computes
-    want = layer_call(L - 1, qd[L - 1], btd, cd).cpu()
+    # the pipelined loop must read back what a plain call computes
+    s = (args.steps - 1) % 2
+    want = layer_call(L - 1, qd[s][L - 1], btd[s], cd[s]).cpu()
     if not torch.equal(out_host[L - 1], want):
         raise SystemExit("e2e read-back differs from a direct call")
     h2d = q_host.numel() * 4 + bt_host[0].numel() * 4 + ctx_host.numel() * 4
