@@ -97,6 +97,30 @@ def test_peer_exchange_layout_and_argument_checks():
     assert _lib.call("pa_ipc_open", None, ctypes.byref(ctypes.c_void_p())) == bad
 
 
+def test_append_kv_and_scaled_writer_argument_checks():
+    bad = _lib.PA_ERR_INVALID_ARGUMENT
+    one = (ctypes.c_void_p * 1)(16)
+    d = ctypes.c_void_p(16)
+    # negative sizes, null pointers with work to do: rejected before any launch
+    assert _lib.call("pa_append_kv", one, one, _lib.PA_DTYPE_F16, d, d, _lib.PA_DTYPE_F32,
+                     d, 4, d, -1, 1, 2, 64, 16, 8, None, None, None, None) == bad
+    assert _lib.call("pa_append_kv", one, one, _lib.PA_DTYPE_F16, d, d, _lib.PA_DTYPE_F32,
+                     None, 4, d, 3, 1, 2, 64, 16, 8, None, None, None, None) == bad
+    assert _lib.call("pa_append_kv", one, one, _lib.PA_DTYPE_F16, d, d, _lib.PA_DTYPE_F32,
+                     d, 4, None, 3, 1, 2, 64, 16, 8, None, None, None, None) == bad
+    # a source dtype the writer does not read, a pool dtype it does not know
+    assert _lib.call("pa_append_kv", one, one, _lib.PA_DTYPE_F16, d, d, _lib.PA_DTYPE_E4M3,
+                     d, 4, d, 3, 1, 2, 64, 16, 8, None, None, None, None) == _lib.PA_ERR_DTYPE
+    assert _lib.call("pa_append_kv", one, one, 17, d, d, _lib.PA_DTYPE_F32,
+                     d, 4, d, 3, 1, 2, 64, 16, 8, None, None, None, None) == _lib.PA_ERR_DTYPE
+    # no sequences: nothing to do
+    assert _lib.call("pa_append_kv", None, None, _lib.PA_DTYPE_F16, None, None,
+                     _lib.PA_DTYPE_F32, None, 4, None, 0, 1, 2, 64, 16, 8, None, None, None,
+                     None) == 0
+    assert _lib.call("pa_write_kv_scaled", None, None, _lib.PA_DTYPE_E4M3, None, None, 9, 0, 0, 0,
+                     None, 4, 0, 10, 1, 12, 64, 16, 10, None, None, None, None) == bad
+
+
 def test_write_kv_argument_checks():
     st = _lib.call("pa_write_kv", None, None, _lib.PA_DTYPE_F16, None, None, 9, 0, 0, 0, None,
                    4, 0, 10, 1, 12, 64, 16, 10, None, None)
