@@ -88,3 +88,23 @@ def test_tensor_core_path_block_size_32_and_padding():
     out = abi_prefill(q, k, v, bt, ctx, 0.088, "bfloat16")
     assert np.all(out[0, :50] == 0)
     assert max_abs(out, orc.prefill(q, k, v, bt, ctx, 0.088, threads=8)) <= 2e-3
+
+
+@pytest.mark.parametrize("dtype,D,BS", [("bfloat16", 128, 16), ("float16", 64, 16),
+                                        ("bfloat16", 128, 32)])
+def test_tensor_core_path_pages_in_order(dtype, D, BS):
+    # pages allocated in order (block id = page index, as a fresh allocator
+    # hands them out): every full KV tile is one run of pool rows; the second
+    # sequence's table is reversed in its second half so runs and scattered
+    # tiles meet in one launch; a ragged context leaves a partial last tile
+    q, k, v, _, ctx = case(46, 2, 260, 8, 4, D, BS, [900, 700], dtype)
+    pages = [-(-int(c) // BS) for c in ctx]
+    bt = np.zeros((2, max(pages)), np.int32)
+    bt[0, :pages[0]] = np.arange(pages[0])
+    second = np.arange(pages[0], pages[0] + pages[1])
+    half = pages[1] // 2
+    second[half:] = second[half:][::-1]
+    bt[1, :pages[1]] = second
+    scale = D ** -0.5
+    out = abi_prefill(q, k, v, bt, ctx, scale, dtype)
+    assert max_abs(out, orc.prefill(q, k, v, bt, ctx, scale, threads=8)) <= 2e-3
