@@ -826,11 +826,21 @@ def run_config5(args) -> None:
     err_b = max_over_ranks(err_b)
     torch.cuda.empty_cache()
 
-    ms_b = timed(decode_b, args.steps)
-    ms_b_nccl = timed(decode_b_nccl, args.steps) if world > 1 else ms_b
-    # the same decode without the exchange: how much the all-gather + merge add
-    ms_b_local = timed(lambda i: ops.paged_attention_v3_lse(qb, kv[0], kv[1], btb[i % R5], ctxb,
-                                                            scale5, 0), args.steps)
+    # the same decode without the exchange shows what the exchange adds; the
+    # three loops alternate over three rounds (median each) so that clock
+    # drift within the run does not bias one of them
+    def decode_b_local(i: int):
+        return ops.paged_attention_v3_lse(qb, kv[0], kv[1], btb[i % R5], ctxb, scale5, 0)
+
+    rounds = {"peer": [], "nccl": [], "local": []}
+    for _ in range(3):
+        rounds["peer"].append(timed(decode_b, args.steps))
+        if world > 1:
+            rounds["nccl"].append(timed(decode_b_nccl, args.steps))
+        rounds["local"].append(timed(decode_b_local, args.steps))
+    ms_b = statistics.median(rounds["peer"])
+    ms_b_nccl = statistics.median(rounds["nccl"]) if world > 1 else ms_b
+    ms_b_local = statistics.median(rounds["local"])
     bytes_b = NT * HKV5 * D5 * 2 * 2 * args.steps
     if world > 1:
         if int(pm.status.item()) != 0:
