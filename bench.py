@@ -437,7 +437,7 @@ def run_fp8(torch, ops, harness, dev, stream, args, peaks) -> dict:
             "tokens_per_s": round(B / (ms * 1e-3), 1), "correctness_gate_max_abs": err,
             "config": f"configs[1] geometry on an e4m3 pool, {L} layers, {REG} cold regions, "
                       "per-KV-head scales",
-            "kernel": "pa::decode::decode_kernel<__nv_fp8_e4m3,64,1> (warp-specialised)"}
+            "kernel": "pa::decode::decode_kernel<__nv_fp8_e4m3,64,1> (light CTA, 32-token stages)"}
 
 
 def correctness_gate(torch, layer_call, pool, q, bt_np, bt_dev, ctx_dev, scale, dev) -> float:
