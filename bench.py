@@ -569,11 +569,21 @@ def cpu_sample(seconds: float, threads: int):
     return gbs, n, sample
 
 
+def simd_note() -> str:
+    """The reference's SIMD CPU lane (arm_cpu, NEON / SVE) runs on aarch64
+    hosts only; its own dispatcher refuses other ISAs."""
+    import platform
+    isa = platform.machine()
+    if isa in ("aarch64", "arm64"):
+        return f"not timed: host ISA is {isa}, but only the scalar lane is built here"
+    return f"unavailable: host ISA is {isa} (the reference's SIMD lane is aarch64 NEON/SVE)"
+
+
 def cpu_baseline(seconds: float) -> dict:
     threads = os.cpu_count() or 1
     gbs, _, sample = cpu_sample(seconds, threads)
     return {"value": round(gbs, 3), "unit": "GB/s", "cores": threads, "kind": "port",
-            "sample": sample}
+            "sample": sample, "simd": simd_note()}
 
 
 def run_config4(torch, ops, harness, dev, stream, args) -> dict:
@@ -898,7 +908,7 @@ def run_reference(args) -> None:
                                "D=64, fp16 values computed in fp32 on the host",
                    "parallelism": f"{threads} host threads, rank 0 only"},
         "cpu_baseline": {"value": round(value, 3), "unit": "GB/s", "cores": threads,
-                         "kind": "port", "sample": sample},
+                         "kind": "port", "sample": sample, "simd": simd_note()},
         "e2e": {"value": round(value, 3), "unit": "GB/s", "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
     }
