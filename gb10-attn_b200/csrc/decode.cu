@@ -59,6 +59,7 @@ constexpr uint32_t kRingBudget = 200 * 1024;  // bytes of stages per CTA
 
 struct Config {
   int QC, G, NS, NGC, nstage, threads, N;
+  int tt;  // tokens per tile (decode::Tile)
   int64_t n_grp;  // run counters for two-level merges (0: single-level merges)
   bool fused;     // plan built by each CTA (no plan kernel)
   uint32_t row_bytes;
@@ -250,7 +251,6 @@ static int check_args(const DecodeArgs& a) {
 // layout.  Needs the current device (SM count, occupancy).
 static int configure(const DecodeArgs& a, Config* c) {
   const int elt = dtype_size(a.dtype);
-  const int tt = tile_tokens(a.dtype);
   const int QPK = (int)(a.H / a.HKV);
   const int epl = decode_elems_per_lane(a.dtype, (int)a.D);
   // Query heads per consumer warp: the largest group whose state fits (each
@@ -258,10 +258,11 @@ static int configure(const DecodeArgs& a, Config* c) {
   // config 3: 8 warps x 4 heads and 16 warps x 2 heads run at the same speed.
   auto pick_g = [&](int qc) {
     const int maxw = decode_max_warps(a.dtype, (int)a.D, qc);
+    const int tq = tile_tokens(a.dtype, qc);
     for (int g = (int)std::min<int64_t>(a.HKV, 64); g >= 1; --g) {
       if (a.HKV % g) continue;
       if (g * (QPK / qc) > maxw) continue;
-      if (2u * tt * (uint32_t)(g * a.D * elt) > kStageCap) continue;
+      if (2u * tq * (uint32_t)(g * a.D * elt) > kStageCap) continue;
       return g;
     }
     return 0;
@@ -279,6 +280,8 @@ static int configure(const DecodeArgs& a, Config* c) {
   (void)best_ns;
   if (G == 0) return PA_ERR_TOO_LARGE;  // QPK / QC beyond one CTA
   const int maxw = decode_max_warps(a.dtype, (int)a.D, QC);
+  const int tt = tile_tokens(a.dtype, QC);
+  c->tt = tt;
   c->QC = QC;
   c->G = G;
   c->NS = G * (QPK / QC);
@@ -370,7 +373,7 @@ int launch(const DecodeArgs& a, void* ws, size_t ws_bytes, cudaStream_t stream) 
   pp.NGC = c.NGC;
   pp.N = c.N;
   pp.empty_fill = a.empty_fill;
-  pp.tt = tile_tokens(a.dtype);
+  pp.tt = c.tt;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = 1;
@@ -403,7 +406,7 @@ int launch(const DecodeArgs& a, void* ws, size_t ws_bytes, cudaStream_t stream) 
   next_epoch(&p.epoch, &p.abort_tag);
   p.empty_fill = a.empty_fill;
   // the start cost is in 16-token tiles: fewer of the larger FP8 tiles
-  p.beta = c.fused ? kStartTiles * kTT / tile_tokens(a.dtype) : 0;
+  p.beta = c.fused ? kStartTiles * kTT / c.tt : 0;
   p.partials = reinterpret_cast<float*>(w + c.off_part);
   p.B = a.B * a.qlen;
   p.qlen = a.qlen;

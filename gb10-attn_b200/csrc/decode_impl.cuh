@@ -6,7 +6,7 @@
 // context, un-normalised partials, log-sum-exp merge (:113-122, :139-165).
 // Different machine mapping:
 //
-//   * Work unit = a tile of kTT = 16 (FP8 pools: 32) consecutive tokens of one sequence for a
+//   * Work unit = a tile of kTT = 16 (FP8 pools with QC == 1: 32) consecutive tokens of one sequence for a
 //     group of G kv heads ("g-chunk").  The NGC * sum_b ceil(ctx_b / 16) tiles
 //     are split into N contiguous ranges, one per CTA (N = SMs x resident CTAs
 //     for automatic splitting), so every SM streams about the same number of
@@ -47,13 +47,19 @@ constexpr int kCountBits = 24;     // arrival count bits of an epoch-tagged coun
 constexpr int kPlanScratchBytes = 272;  // scan scratch ahead of the fused plan tables
 constexpr float kNegBig = -3.0e38f;  // the reference's "minus infinity" (paged_attn_v3.cu:20)
 
-// FP8 pools use 32-token stages: the bytes of a 16-bit pool's 16 tokens, and
-// twice the rows per consumer lane for each stage wait.
-template <typename T>
+// FP8 pools with one query head per KV row and warp (QC == 1) use 32-token
+// stages: the bytes of a 16-bit pool's 16 tokens, and twice the rows per
+// consumer lane for each stage wait (3.72 vs 3.01 TB/s at configs[1]
+// geometry).  With several query heads per KV row the consumer work per stage
+// already dominates, and 16-token stages measured faster (88.0 vs 108.7 us
+// per call at configs[2] geometry).
+template <typename T, int QC>
 struct Tile {
-  static constexpr int TT = sizeof(T) == 1 ? 2 * kTT : kTT;
+  static constexpr int TT = (sizeof(T) == 1 && QC == 1) ? 2 * kTT : kTT;
 };
-inline int tile_tokens(int dtype) { return dtype_size(dtype) == 1 ? 2 * kTT : kTT; }
+inline int tile_tokens(int dtype, int qc) {
+  return (dtype_size(dtype) == 1 && qc == 1) ? 2 * kTT : kTT;
+}
 
 struct Params {
   float* out;                    // [B, H, D]
@@ -107,8 +113,8 @@ struct __align__(16) StageHeader {
 };
 constexpr int kFirst = 1, kLast = 2, kEnd = 4, kCtaLast = 8;
 
-// Lane geometry for element type T and head_dim D.
-template <typename T, int D>
+// Lane geometry for element type T and head_dim D (TT tokens per stage).
+template <typename T, int D, int TT = kTT>
 struct Geo {
   static constexpr int VEC = Chunk<T>::N;                 // elements per 16 B
   static constexpr int CH = D / VEC;                      // 16 B chunks per row
@@ -116,8 +122,8 @@ struct Geo {
   static constexpr int NCH = CH / R;                      // chunks per lane
   static constexpr int EPL = NCH * VEC;                   // elements per lane
   static constexpr int NRG = 32 / R;                      // row groups per warp
-  static constexpr int TPR = Tile<T>::TT / NRG;          // tokens per row group per stage
-  static_assert(D % VEC == 0 && CH % R == 0 && 32 % R == 0 && NRG <= Tile<T>::TT, "geometry");
+  static constexpr int TPR = TT / NRG;                    // tokens per row group per stage
+  static_assert(D % VEC == 0 && CH % R == 0 && 32 % R == 0 && NRG <= TT, "geometry");
 };
 
 // CTA shape of a (T, D, QC) instantiation, by the per-lane register state
@@ -357,13 +363,13 @@ __device__ __forceinline__ void merge_pieces_wide(PtrFn ptr, int64_t c0, int64_t
 template <typename T, int D, int QC>
 __global__ void __launch_bounds__(Limits<T, D, QC>::THREADS, 1)
     decode_kernel(const __grid_constant__ Params p) {
-  using G_ = Geo<T, D>;
+  constexpr int TT = Tile<T, QC>::TT;
+  using G_ = Geo<T, D, TT>;
   constexpr int VEC = G_::VEC, R = G_::R, NCH = G_::NCH, EPL = G_::EPL;
   constexpr int NRG = G_::NRG, TPR = G_::TPR;
 
   extern __shared__ __align__(128) unsigned char smem[];
   const int nstage = p.nstage;
-  constexpr int TT = Tile<T>::TT;
   const uint32_t stage_bytes = 2u * TT * p.row_bytes;
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + (size_t)nstage * stage_bytes);
   uint64_t* empty = full + nstage;
@@ -399,7 +405,7 @@ __global__ void __launch_bounds__(Limits<T, D, QC>::THREADS, 1)
     int32_t* to_s = reinterpret_cast<int32_t*>(plan_base + kPlanScratchBytes);
     int32_t* nt_s = to_s + p.B + 1;
     int32_t* nz_s = nt_s + p.B;
-    fused_plan<D, Tile<T>::TT>(p, to_s, nt_s, nz_s, reinterpret_cast<long long*>(plan_base));
+    fused_plan<D, TT>(p, to_s, nt_s, nz_s, reinterpret_cast<long long*>(plan_base));
     tile_off = to_s;
     ntok_s = nt_s;
     ne_s = nz_s;
