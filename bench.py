@@ -25,6 +25,11 @@ N > 1      one process per GPU (torchrun); each rank runs the same per-GPU
 lines: the batch shard at 64 sequences x ctx 8192 per GPU, and one 1,048,576-
 token GQA sequence split over the ranks with its partials merged over NVLink.
 
+extra      (one GPU) the config-3 GQA decode, the config-4 prefill and its
+           write_kv, and the configs[1] decode on an FP8 E4M3 pool, each as
+           its own object with its roofline fraction; --workload config3 /
+           config4 / fp8 run one of them alone (profiler captures).
+
 --impl reference times the reference's scalar FP32 CPU decode (the oracle's
 restatement of gb10-attn rocm/hip/paged_attn_v1_hip.cpp:104-141; the HIP file
 itself does not build here) on the host cores, on a bounded sample of the
