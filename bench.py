@@ -64,6 +64,22 @@ def _env_rank():
             int(os.environ.get("WORLD_SIZE", 1)))
 
 
+# the phase each rank is in, named in its error line if it fails
+_STAGE = ["start"]
+
+
+def _stage(name: str) -> None:
+    _STAGE[0] = name
+
+
+def _error_line(msg: str, impl: str) -> None:
+    """One flushed JSON line on stdout from the failing rank (torchrun's
+    summary on stderr would bury a message printed there)."""
+    rank, _, world = _env_rank()
+    print(json.dumps({"impl": impl, "error": msg[-2000:], "rank": rank, "world_size": world,
+                      "where": _STAGE[0]}), flush=True)
+
+
 def _peaks() -> dict:
     p = REPO / "MEASURED_PEAKS.json"
     if p.exists():
@@ -76,15 +92,23 @@ def _peaks() -> dict:
 
 
 def _profile_traffic(kernel_key: str) -> float | None:
-    """DRAM bytes per launch of the decode kernel from the committed ncu
-    summary (a line 'traffic_bytes_per_launch: N' in profiles/*.md)."""
-    for p in sorted((REPO / "profiles").glob(f"{kernel_key}*.md")):
-        for line in p.read_text().splitlines():
-            if line.strip().startswith("traffic_bytes_per_launch:"):
-                try:
-                    return float(line.split(":", 1)[1].strip().split()[0])
-                except ValueError:
-                    return None
+    """DRAM bytes per launch of a kernel from its committed ncu summary (a
+    line 'traffic_bytes_per_launch: N' in profiles/<kernel_key>.md): ncu
+    cannot run inside the timed process, so the figure comes from the capture
+    of the same build, and the line names that file beside it."""
+    return _profile_value(kernel_key, "traffic_bytes_per_launch")
+
+
+def _profile_value(kernel_key: str, key: str) -> float | None:
+    p = REPO / "profiles" / f"{kernel_key}.md"
+    if not p.exists():
+        return None
+    for line in p.read_text().splitlines():
+        if line.strip().startswith(key + ":"):
+            try:
+                return float(line.split(":", 1)[1].strip().split()[0])
+            except ValueError:
+                return None
     return None
 
 
@@ -163,10 +187,12 @@ def run_b200(args) -> None:
     rank, local, world = _env_rank()
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
+    _stage("init_process_group")
     if world > 1:
         import datetime
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                 device_id=dev)
+    _stage("pools")
 
     gen = torch.Generator(device=dev)
     gen.manual_seed(1234 + rank)
@@ -199,14 +225,17 @@ def run_b200(args) -> None:
         for layer in range(L):
             outs[layer] = layer_call(layer, q_dev[layer], bt, ctx_dev)
 
+    _stage("correctness_gate")
     ref_err = correctness_gate(torch, layer_call, pools[0], q_dev[0], tables[0], bt_dev[0],
                                ctx_dev, scale, dev)
     if ref_err > 2e-3:
         raise SystemExit(f"correctness gate failed: max-abs {ref_err}")
 
+    _stage("warmup")
     for i in range(args.warmup):
         step(i)
     torch.cuda.synchronize()
+    _stage("timed")
 
     # --- kernel-only timed region -----------------------------------------
     if world > 1:
@@ -224,6 +253,7 @@ def run_b200(args) -> None:
     t_ms = ev0.elapsed_time(ev1)
 
     # --- per-launch decode time (same stream, events around each call) -----
+    _stage("launch_timing")
     n_launch = min(L * 4, max(L * args.steps, 4))
     evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
            for _ in range(n_launch)]
@@ -237,6 +267,7 @@ def run_b200(args) -> None:
     launch_ms = statistics.mean(a.elapsed_time(b_) for a, b_ in evs)
 
     # --- end to end through the public API with host buffers ---------------
+    _stage("e2e")
     if args.no_e2e:
         e2e_ms, h2d, d2h = float("nan"), 0, 0
     else:
@@ -244,6 +275,7 @@ def run_b200(args) -> None:
                                    stream, world, L, REGIONS)
 
     # max over ranks
+    _stage("max_over_ranks")
     times = torch.tensor([t_ms, e2e_ms, launch_ms], dtype=torch.float64, device=dev)
     if world > 1:
         dist.all_reduce(times, op=dist.ReduceOp.MAX)
@@ -286,7 +318,10 @@ def run_b200(args) -> None:
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1),
                      "peak": peaks["hbm_gbs"], "unit": "GB/s",
                      "frac": round(achieved / peaks["hbm_gbs"], 4),
-                     "traffic": traffic, "peak_source": peaks["src"],
+                     "traffic": traffic,
+                     "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum, "
+                                       "profiles/decode_kernel_config2.md",
+                     "peak_source": peaks["src"],
                      "kernel": "pa::decode::decode_kernel<__half,64,1> (plan built in-kernel)",
                      "bytes_per_launch": bytes_per_call,
                      "launch_us": round(call_ms * 1e3, 2),
@@ -296,6 +331,7 @@ def run_b200(args) -> None:
     if world == 1 and not args.no_extra:
         del pools, outs
         torch.cuda.empty_cache()
+        _stage("extra")
         line["extra"] = {"config3_gqa_long_context": run_config3(torch, ops, harness, dev,
                                                                  stream, args, peaks),
                          "config4_prefill": run_config4(torch, ops, harness, dev, stream, args),
@@ -304,7 +340,15 @@ def run_b200(args) -> None:
         fp8 = line["extra"]["fp8_kv_config2_geometry"]
         fp8["tokens_per_s_vs_fp16_line"] = round(
             fp8["tokens_per_s"] / line["config"]["tokens_per_s"], 3)
+    if world > 1 and not args.no_extra:
+        # BASELINE.json configs[4] on the same ranks: the batch shard at
+        # ctx 8192 and the 1 M-token sequence shard with its exchange
+        del pools, outs
+        torch.cuda.empty_cache()
+        line["extra"] = {"config5_multi_gpu": measure_config5(torch, dist, args, rank, world,
+                                                              dev, peaks)}
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        _stage("cpu_baseline")
         line["cpu_baseline"] = cpu_baseline(args.cpu_seconds)
     if world > 1:
         dist.barrier()
@@ -321,7 +365,7 @@ def run_config3(torch, ops, harness, dev, stream, args, peaks) -> dict:
     4 disjoint regions rotated per call (each call reads ~0.55 GB)."""
     H3, HKV3, D3, BS3, B3, NB3, REG = 32, 8, 128, 16, 8, args.pool_blocks, 4
     rng = np.random.default_rng(2026)
-    ctx = rng.integers(1024, 32769, size=B3).astype(np.int32) * int(args.ctx_scale)
+    ctx = rng.integers(1024, 32769, size=B3).astype(np.int32)
     need = [int(-(-c // BS3)) for c in ctx]
     gen = torch.Generator(device=dev)
     gen.manual_seed(99)
@@ -368,10 +412,10 @@ def run_config3(torch, ops, harness, dev, stream, args, peaks) -> dict:
     return {"value": round(gbs, 1), "unit": "GB/s",
             "pct_of_measured_hbm_peak": round(100 * gbs / peaks["hbm_gbs"], 1),
             "traffic_bytes_per_launch": _profile_traffic("decode_kernel_config3"),
+            "traffic_source": "profiles/decode_kernel_config3.md",
             "us_per_call": round(ms * 1e3, 2), "bytes_per_call": per_call,
             "calls": n, "context_lens": ctx.tolist(), "pool_elements_per_tensor": NB3 * BS3 * HKV3 * D3,
             "tokens_per_s": round(B3 / (ms * 1e-3), 1), "correctness_gate_max_abs": err,
-            "ctx_scale": int(args.ctx_scale),
             "kernel": "pa::decode::decode_kernel<__nv_bfloat16,128,4> (warp-specialised)"}
 
 
@@ -538,7 +582,10 @@ def run_e2e(torch, dist, args, layer_call, q_dev, tables, ctx_np, dev, stream, w
     s = (args.steps - 1) % 2
     want = layer_call(L - 1, qd[s][L - 1], btd[s], cd[s]).cpu()
     if not torch.equal(out_host[L - 1], want):
-        raise SystemExit("e2e read-back differs from a direct call")
+        diff = float((out_host[L - 1] - want).abs().nan_to_num(float("inf")).max())
+        raise SystemExit(f"e2e read-back differs from a direct call (max-abs {diff:.3e}; "
+                         "the decode is bit-deterministic, so any difference is an ordering "
+                         "error)")
     h2d = q_host.numel() * 4 + bt_host[0].numel() * 4 + ctx_host.numel() * 4
     d2h = out_host.numel() * 4
     return e0.elapsed_time(e1), h2d, d2h
@@ -548,6 +595,27 @@ def run_e2e(torch, dist, args, layer_call, q_dev, tables, ctx_np, dev, stream, w
 # the CPU reference arm / baseline
 # ---------------------------------------------------------------------------
 
+_CPU_CASE: list = []
+
+
+def _cpu_case():
+    """The config-2 layer inputs for the CPU timings, made once: N(0,1) q
+    and fp16-representable K/V (fp32 arrays), a seeded permutation of the
+    4096 pages as block table.  torch's CPU generator (multi-threaded) makes
+    the 200 M values in a fraction of numpy's time; the values do not affect
+    the timing."""
+    if not _CPU_CASE:
+        import torch
+        g = torch.Generator().manual_seed(7)
+        nb = B * CTX // BS
+        q = torch.randn((B, H, D), generator=g).numpy()
+        k = torch.randn((nb, BS, HKV, D), generator=g).half().float().numpy()
+        v = torch.randn((nb, BS, HKV, D), generator=g).half().float().numpy()
+        bt = np.random.default_rng(7).permutation(nb).astype(np.int32).reshape(B, CTX // BS)
+        _CPU_CASE.append((q, k, v, bt, np.full(B, CTX, np.int32)))
+    return _CPU_CASE[0]
+
+
 def cpu_sample(seconds: float, threads: int):
     """Times the oracle restatement of the reference's scalar FP32 CPU decode
     on layer calls of the config-2 workload (fp16 values upcast to fp32, as
@@ -556,9 +624,7 @@ def cpu_sample(seconds: float, threads: int):
     from oracle import oracle as orc
     from pa_b200 import harness
 
-    q, k, v, bt, ctx = orc.make_decode_case(7, B, H, HKV, D, BS, CTX)
-    k = orc.round_to(k, "float16")
-    v = orc.round_to(v, "float16")
+    q, k, v, bt, ctx = _cpu_case()
     orc.decode(q[:1], k, v, bt[:1], ctx[:1], D ** -0.5, threads=1)  # warm
     per_call = harness.decode_bytes(ctx, H, HKV, D, 2, BS)
     n, t0 = 0, time.perf_counter()
@@ -584,11 +650,52 @@ def simd_note() -> str:
     return f"unavailable: host ISA is {isa} (the reference's SIMD lane is aarch64 NEON/SVE)"
 
 
+def cpu_model() -> str:
+    try:
+        for line in Path("/proc/cpuinfo").read_text().splitlines():
+            if line.lower().startswith("model name"):
+                return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    import platform
+    return platform.processor() or platform.machine()
+
+
+def arm_bench_scalar() -> dict:
+    """The reference's own CPU microbenchmark, arm_cpu's arm_attn_bench
+    (built from its sources into oracle/_ref/ by oracle/build_ref.py): scalar
+    scores + softmax of one 2048-token, 64-dim head (no V, no paging)."""
+    exe = REPO / "oracle" / "_ref" / "arm_attn_bench"
+    cmd = ["--backend", "scalar", "--tokens", "2048", "--dim", "64", "--csv"]
+    if not exe.exists():
+        return {"unavailable": "oracle/_ref/arm_attn_bench was not built (reference sources "
+                               "absent at build time)"}
+    try:
+        r = subprocess.run([str(exe), *cmd], capture_output=True, text=True, timeout=120)
+    except (OSError, subprocess.TimeoutExpired) as e:
+        return {"unavailable": f"{type(e).__name__}: {e}"}
+    lines = [x for x in r.stdout.splitlines() if x.strip()]
+    if r.returncode != 0 or len(lines) < 2:
+        return {"unavailable": f"exit {r.returncode}: {r.stderr.strip()[-200:]}"}
+    row = dict(zip(lines[0].split(","), lines[1].split(",")))
+    return {"command": "arm_attn_bench " + " ".join(cmd), "backend": row.get("backend"),
+            "effective_key_gbs": float(row["effective_key_gbs"]),
+            "ns_per_dot": float(row["ns_per_dot"]), "gflops": float(row["gflops"]),
+            "seconds": float(row["seconds"]), "iters": int(row["iters"]), "threads": 1}
+
+
 def cpu_baseline(seconds: float) -> dict:
+    """The reference's scalar FP32 CPU decode (the oracle's restatement) on
+    the config-2 workload, single-threaded as the reference runs it and on
+    every host thread (one (sequence, head) per task), plus the reference's
+    own arm_attn_bench scalar run; about `seconds` of CPU work in all."""
     threads = os.cpu_count() or 1
-    gbs, _, sample = cpu_sample(seconds, threads)
+    gbs1, _, sample1 = cpu_sample(seconds / 2, 1)
+    gbs, _, sample = cpu_sample(seconds / 2, threads)
     return {"value": round(gbs, 3), "unit": "GB/s", "cores": threads, "kind": "port",
-            "sample": sample, "simd": simd_note()}
+            "sample": sample, "threads": threads, "cpu_model": cpu_model(),
+            "single_thread": {"value": round(gbs1, 3), "unit": "GB/s", "sample": sample1},
+            "arm_attn_bench_scalar": arm_bench_scalar(), "simd": simd_note()}
 
 
 def run_config4(torch, ops, harness, dev, stream, args) -> dict:
@@ -710,30 +817,45 @@ def run_fp8_only(args) -> None:
 
 
 def run_config5(args) -> None:
-    """BASELINE.json configs[4], one process per GPU (torchrun).  (A) batch
-    shard: gpt2 fp16 decode, 64 sequences of ctx 8192 per GPU, `--layers`
-    layer pools with 2 cold regions, no collective; (B) one sequence of
-    1,048,576 tokens, 32 query / 8 KV heads, D=128, bf16, its token range split
-    evenly over the ranks: each decodes its range into its exchange buffer and
-    one launch merges the ranks' partials over peer memory
-    (pa_b200.dist.PeerMerge); the NCCL all-gather variant
-    (sequence_sharded_decode) is timed beside it.  Times are the max over ranks;
-    the B output is checked against per-rank dense fp32 partials merged with
-    the same rule."""
+    """--workload config5: the configs[4] lines alone (torchrun)."""
     import datetime
 
     import torch
     import torch.distributed as dist
 
-    from pa_b200 import dist as padist
-    from pa_b200 import harness, ops
-
     rank, local, world = _env_rank()
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
+    _stage("init_process_group")
     if world > 1:
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
-    peaks = _peaks()
+    r = measure_config5(torch, dist, args, rank, world, dev, _peaks())
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank == 0:
+        line = {"metric": METRIC, "workload": "configs[4]", "n_gpus": world,
+                "value": r["batch_shard"]["value"], "unit": "GB/s", "steps": args.steps,
+                "warmup": args.warmup, "scaling": "weak", "higher_is_better": True,
+                "data": "synthetic N(0,1) KV pools and q, seeded", **r}
+        print(json.dumps(line), flush=True)
+
+
+def measure_config5(torch, dist, args, rank, world, dev, peaks) -> dict:
+    """BASELINE.json configs[4], one process per GPU, called on every rank
+    (the process group, if world > 1, is the caller's).  (A) batch shard:
+    gpt2 fp16 decode, 64 sequences of ctx 8192 per GPU, `--layers` layer pools
+    with 2 cold regions, no collective; (B) one sequence of 1,048,576 tokens,
+    32 query / 8 KV heads, D=128, bf16, its token range split evenly over the
+    ranks: each decodes its range into its exchange buffer and one launch
+    merges the ranks' partials over peer memory (pa_b200.dist.PeerMerge); the
+    NCCL all-gather variant (sequence_sharded_decode) and the decode alone are
+    timed beside it.  Times are the max over ranks; the B output is checked
+    against per-rank dense fp32 partials merged with the same rule.  Returns
+    the result object (the same on every rank)."""
+    from pa_b200 import dist as padist
+    from pa_b200 import harness, ops
+
     stream = torch.cuda.current_stream()
     gen = torch.Generator(device=dev)
     gen.manual_seed(5000 + rank)
@@ -759,6 +881,7 @@ def run_config5(args) -> None:
         return max_over_ranks(e0.elapsed_time(e1))
 
     # (A) batch shard ------------------------------------------------------
+    _stage("config5.batch_shard")
     BA, CTXA, RA, LA = 64, 8192, 2, args.layers
     nb = BA * (CTXA // BS) * RA
     pools = []
@@ -785,6 +908,7 @@ def run_config5(args) -> None:
     torch.cuda.empty_cache()
 
     # (B) one long sequence over the ranks ----------------------------------
+    _stage("config5.sequence_shard")
     NT, H5, HKV5, D5, R5 = 1 << 20, 32, 8, 128, 2
     nt = NT // world  # this rank's token range [rank * nt, (rank + 1) * nt)
     need = nt // BS
@@ -839,6 +963,8 @@ def run_config5(args) -> None:
         if int(pm.status.item()) != 0:
             raise SystemExit(f"config5: device status {int(pm.status.item())}")
     err_b = max_over_ranks(err_b)
+    if err_b > 2e-3:
+        raise SystemExit(f"config5 sequence-shard gate failed: max-abs {err_b}")
     torch.cuda.empty_cache()
 
     # the same decode without the exchange shows what the exchange adds; the
@@ -861,35 +987,29 @@ def run_config5(args) -> None:
         if int(pm.status.item()) != 0:
             raise SystemExit(f"config5: device status {int(pm.status.item())}")
         pm.close()
-        dist.barrier()
-        dist.destroy_process_group()
-    if rank == 0:
-        line = {
-            "metric": METRIC, "workload": "configs[4]", "n_gpus": world,
-            "value": round(gbs_a, 1), "unit": "GB/s", "steps": args.steps,
-            "warmup": args.warmup, "scaling": "weak", "higher_is_better": True,
-            "data": "synthetic N(0,1) KV pools and q, seeded",
-            "batch_shard": {
-                "value": round(gbs_a, 1), "unit": "GB/s",
-                "pct_of_measured_hbm_peak": round(100 * gbs_a / world / peaks["hbm_gbs"], 1),
-                "config": f"gpt2 fp16, {BA} sequences x ctx {CTXA} per GPU, {LA} layers, "
-                          f"{RA} cold regions; no collective",
-                "ms_per_step": round(ms_a / args.steps, 4),
-                "tokens_per_s": round(BA * world * args.steps / (ms_a * 1e-3), 1)},
-            "sequence_sharded": {
-                "value": round(bytes_b / (ms_b * 1e-3) / 1e9, 1), "unit": "GB/s",
-                "pct_of_measured_hbm_peak": round(100 * bytes_b / (ms_b * 1e-3) / 1e9 / world
-                                                  / peaks["hbm_gbs"], 1),
-                "config": f"1 sequence of {NT} tokens, 32q/8kv, D=128, bf16, "
-                          f"{nt} tokens ({nt * HKV5 * D5 * 4 / 1e9:.2f} GB K+V) per GPU",
-                "us_per_step": round(ms_b / args.steps * 1e3, 2),
-                "us_per_step_local_only": round(ms_b_local / args.steps * 1e3, 2),
-                "exchange": "peer memory: flags + peer loads + LSE merge in one launch "
-                            "(pa_merge_peer_partials)" if world > 1 else "none (one GPU)",
-                "us_per_step_nccl_all_gather": round(ms_b_nccl / args.steps * 1e3, 2),
-                "correctness_gate_max_abs": err_b},
-        }
-        print(json.dumps(line), flush=True)
+    gbs_b = bytes_b / (ms_b * 1e-3) / 1e9
+    return {
+        "batch_shard": {
+            "value": round(gbs_a, 1), "unit": "GB/s",
+            "pct_of_measured_hbm_peak": round(100 * gbs_a / world / peaks["hbm_gbs"], 1),
+            "config": f"gpt2 fp16, {BA} sequences x ctx {CTXA} per GPU, {LA} layers, "
+                      f"{RA} cold regions; no collective",
+            "ms_per_step": round(ms_a / args.steps, 4),
+            "tokens_per_s": round(BA * world * args.steps / (ms_a * 1e-3), 1)},
+        "sequence_sharded": {
+            "value": round(gbs_b, 1), "unit": "GB/s",
+            "pct_of_measured_hbm_peak": round(100 * gbs_b / world / peaks["hbm_gbs"], 1),
+            "config": f"1 sequence of {NT} tokens, 32q/8kv, D=128, bf16, "
+                      f"{nt} tokens ({nt * HKV5 * D5 * 4 / 1e9:.2f} GB K+V) per GPU",
+            "us_per_step": round(ms_b / args.steps * 1e3, 2),
+            "us_per_step_local_only": round(ms_b_local / args.steps * 1e3, 2),
+            "exchange_us_per_step": round((ms_b - ms_b_local) / args.steps * 1e3, 2),
+            "exchange": "peer memory: flags + peer loads + LSE merge in one launch "
+                        "(pa_merge_peer_partials)" if world > 1 else "none (one GPU)",
+            "us_per_step_nccl_all_gather": round(ms_b_nccl / args.steps * 1e3, 2),
+            "nccl_exchange_us_per_step": round((ms_b_nccl - ms_b_local) / args.steps * 1e3, 2),
+            "correctness_gate_max_abs": err_b},
+    }
 
 
 def run_reference(args) -> None:
@@ -913,7 +1033,8 @@ def run_reference(args) -> None:
                                "D=64, fp16 values computed in fp32 on the host",
                    "parallelism": f"{threads} host threads, rank 0 only"},
         "cpu_baseline": {"value": round(value, 3), "unit": "GB/s", "cores": threads,
-                         "kind": "port", "sample": sample, "simd": simd_note()},
+                         "kind": "port", "sample": sample, "threads": threads,
+                         "cpu_model": cpu_model(), "simd": simd_note()},
         "e2e": {"value": round(value, 3), "unit": "GB/s", "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
     }
@@ -929,34 +1050,47 @@ def main() -> None:
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--ref-step-seconds", type=float, default=3.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--layers", type=int, default=12, help="fewer layers: profiler captures only")
-    ap.add_argument("--regions", type=int, default=4, help="cold block regions in rotation")
+    ap.add_argument("--layers", type=int, default=12,
+                    help="layer pools per decode step (configs[1]: 12)")
+    ap.add_argument("--cold-pools", "--regions", dest="regions", type=int, default=4,
+                    help="disjoint KV block regions rotated step by step (the reference "
+                         "harness's --cold-pools)")
     ap.add_argument("--no-e2e", action="store_true", help="skip the host-buffer e2e leg")
     ap.add_argument("--no-extra", action="store_true", help="skip the config-3 GQA measurement")
     ap.add_argument("--workload", choices=["config2", "config3", "config4", "config5", "fp8"],
                     default="config2",
-                    help="config3 / config4 / fp8 run the GQA decode / the prefill / the FP8-pool "
-                         "decode alone (profiling); config5 the multi-GPU batch-shard + "
-                         "sequence-shard lines (torchrun)")
-    ap.add_argument("--ctx-scale", type=int, default=1,
-                    help="config3 only: multiply the seeded context lengths (fixed-cost study)")
+                    help="config2 (default): the headline line with every extra; config3 / "
+                         "config4 / config5 / fp8: one BASELINE config alone (the GQA decode, "
+                         "the prefill, the multi-GPU lines under torchrun, the FP8-pool decode)")
     ap.add_argument("--pool-blocks", type=int, default=140_000,
                     help="config-3 pool blocks (140000: each K/V tensor > 2^31 elements)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
-    if args.impl == "reference":
-        run_reference(args)
-    elif args.workload == "config3":
-        run_config3_only(args)
-    elif args.workload == "config4":
-        run_config4_only(args)
-    elif args.workload == "config5":
-        run_config5(args)
-    elif args.workload == "fp8":
-        run_fp8_only(args)
-    else:
-        run_b200(args)
+    try:
+        if args.impl == "reference":
+            run_reference(args)
+        elif args.workload == "config3":
+            run_config3_only(args)
+        elif args.workload == "config4":
+            run_config4_only(args)
+        elif args.workload == "config5":
+            run_config5(args)
+        elif args.workload == "fp8":
+            run_fp8_only(args)
+        else:
+            run_b200(args)
+    except SystemExit as e:
+        if e.code in (None, 0):
+            raise
+        _error_line(str(e.code), args.impl)
+        sys.exit(1)
+    except BaseException as e:  # noqa: BLE001 -- every failure gets its line
+        import traceback
+        tb = traceback.extract_tb(e.__traceback__)
+        at = f" at {Path(tb[-1].filename).name}:{tb[-1].lineno}" if tb else ""
+        _error_line(f"{type(e).__name__}: {e}{at}", args.impl)
+        sys.exit(1)
 
 
 if __name__ == "__main__":

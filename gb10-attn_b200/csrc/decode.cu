@@ -80,6 +80,10 @@ constexpr int kStartTiles = 6;
 // Launch epoch: tags the merge counters and the abort flag of one launch, so
 // no kernel has to zero them.  40 bits, never 0; starts from the clock so two
 // processes sharing a workspace layout do not replay each other's tags.
+// CAS rounds before a merge arrival gives up (pa_set_merge_arrive_rounds).
+constexpr int kArriveRounds = 1 << 20;
+static std::atomic<int> g_arrive_rounds{kArriveRounds};
+
 static void next_epoch(unsigned long long* epoch, int32_t* abort_tag) {
   static std::atomic<unsigned long long> ctr{
       (unsigned long long)std::chrono::steady_clock::now().time_since_epoch().count() * 2654435761ull};
@@ -404,6 +408,7 @@ int launch(const DecodeArgs& a, void* ws, size_t ws_bytes, cudaStream_t stream) 
   p.grp_counters = c.n_grp ? p.counters + (int64_t)c.NGC * pp.B * c.NS : nullptr;
   p.abort_flag = reinterpret_cast<int32_t*>(w + c.off_abort);
   next_epoch(&p.epoch, &p.abort_tag);
+  p.arrive_rounds = g_arrive_rounds.load(std::memory_order_relaxed);
   p.empty_fill = a.empty_fill;
   // the start cost is in 16-token tiles: fewer of the larger FP8 tiles
   p.beta = c.fused ? kStartTiles * kTT / c.tt : 0;
@@ -516,6 +521,10 @@ __global__ void validate_kernel(const int32_t* __restrict__ bt, const int32_t* _
 // ---------------------------------------------------------------------------
 
 using pa::decode::DecodeArgs;
+
+extern "C" int pa_set_merge_arrive_rounds(int rounds) {
+  return pa::decode::g_arrive_rounds.exchange(rounds < 0 ? pa::decode::kArriveRounds : rounds);
+}
 
 extern "C" int64_t pa_choose_num_splits(int64_t num_seqs, int64_t num_heads,
                                         int64_t max_context) {

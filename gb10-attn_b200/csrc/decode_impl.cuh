@@ -79,6 +79,7 @@ struct Params {
   unsigned long long* counters;      // [NGC * B * NS]
   unsigned long long* grp_counters;  // [N * 2 * NS] arrivals per run of kGroup pieces, or null
   unsigned long long epoch;          // this launch's tag (nonzero, < 2^40)
+  int32_t arrive_rounds;             // CAS rounds before an arrival gives up
   int32_t* abort_flag;           // holds abort_tag once any pipeline wait timed out
   int32_t abort_tag;
   float empty_fill;              // rows of empty sequences (fused plan)
@@ -170,16 +171,20 @@ __host__ __device__ __forceinline__ int64_t cta_of(int64_t t, int64_t T_all, int
 // One arrival on an epoch-tagged counter (value = epoch << kCountBits |
 // count); returns the arrivals of this launch before it.  A value left by an
 // earlier launch (another epoch) counts as zero, so counters are never reset.
-__device__ __forceinline__ int epoch_arrive(unsigned long long* counter, unsigned long long epoch) {
+// Gives up after `rounds` failed compare-and-swap rounds and returns -1: the
+// arrival is not counted, so no warp completes that merge, and the caller
+// writes NaN rows and reports PA_DEVERR_MERGE instead.
+__device__ __forceinline__ int epoch_arrive(unsigned long long* counter, unsigned long long epoch,
+                                            int rounds) {
   unsigned long long v = *reinterpret_cast<volatile unsigned long long*>(counter);
-  for (int it = 0; it < (1 << 20); ++it) {  // lock-free: one CAS wins per round
+  for (int it = 0; it < rounds; ++it) {  // lock-free: one CAS wins per round
     const bool same = (v >> kCountBits) == epoch;
     const unsigned long long nv = same ? v + 1 : ((epoch << kCountBits) | 1ull);
     const unsigned long long prev = atomicCAS(counter, v, nv);
     if (prev == v) return same ? (int)(v & ((1ull << kCountBits) - 1)) : 0;
     v = prev;
   }
-  return -1;  // never settled: no merge from this arrival
+  return -1;  // never settled: the arrival is not counted
 }
 
 // The plan of one launch built by every CTA in shared memory (B <= kFusedRows
@@ -257,17 +262,19 @@ __device__ __forceinline__ void fused_plan(const Params& p, int32_t* tile_off_s,
 
 // Log-sum-exp merge of the partial states at ptr(c0), ptr(c0 + stride), ...
 // (count of them; layout [QC][D] un-normalised O, then QC maxima, then QC
-// sums).  One warp: lane k takes the (m, l) of states k, k + 32, ... so the
-// maxima and weights cost one round trip per 32 states; the O rows are then
-// read a few states at a time with the weights broadcast.  Every lane ends
-// with the merged maxima mg, sums lg and elements lane + 32k of O in o[k].
+// sums).  One warp.  The result is a fixed function of the states: the
+// maxima first (exact), then every state's weight w_k = 2^(m_k - mg) and
+// o += O_k * w_k by fmaf in state order, and l summed per lane over states
+// k = lane, lane + 32, ... before one xor-tree reduction.  Both variants below
+// follow exactly that order, so whichever warp happens to merge a sequence
+// (the last to arrive, which varies from launch to launch) writes the same
+// bits.  Every lane ends with the merged maxima mg, sums lg and elements
+// lane + 32k of O in o[k].
 template <int QC, int D, typename PtrFn>
-__device__ __forceinline__ void merge_pieces(PtrFn ptr, int64_t c0, int64_t stride, int64_t count,
-                                             int lane, float (&o)[QC * D / 32], float (&mg)[QC],
-                                             float (&lg)[QC]) {
-  constexpr int PER = QC * D / 32;
+__device__ __forceinline__ void merge_maxima(PtrFn ptr, int64_t c0, int64_t stride, int64_t count,
+                                             int lane, float (&mg)[QC]) {
 #pragma unroll
-  for (int j = 0; j < QC; ++j) { mg[j] = kNegBig; lg[j] = 0.f; }
+  for (int j = 0; j < QC; ++j) mg[j] = kNegBig;
   for (int64_t k = lane; k < count; k += 32) {
     const float* pc = ptr(c0 + k * stride);
 #pragma unroll
@@ -277,6 +284,27 @@ __device__ __forceinline__ void merge_pieces(PtrFn ptr, int64_t c0, int64_t stri
   for (int j = 0; j < QC; ++j)
 #pragma unroll
     for (int off = 16; off >= 1; off >>= 1) mg[j] = fmaxf(mg[j], __shfl_xor_sync(0xffffffffu, mg[j], off));
+}
+
+template <int QC>
+__device__ __forceinline__ void reduce_sums(float (&lg)[QC]) {
+#pragma unroll
+  for (int j = 0; j < QC; ++j)
+#pragma unroll
+    for (int off = 16; off >= 1; off >>= 1) lg[j] += __shfl_xor_sync(0xffffffffu, lg[j], off);
+}
+
+// Lane k computes the weights of states k, k + 32, ... and broadcasts them;
+// the O rows are read one state at a time (few registers: usable inside the
+// consumer loop).
+template <int QC, int D, typename PtrFn>
+__device__ __forceinline__ void merge_pieces(PtrFn ptr, int64_t c0, int64_t stride, int64_t count,
+                                             int lane, float (&o)[QC * D / 32], float (&mg)[QC],
+                                             float (&lg)[QC]) {
+  constexpr int PER = QC * D / 32;
+  merge_maxima<QC, D>(ptr, c0, stride, count, lane, mg);
+#pragma unroll
+  for (int j = 0; j < QC; ++j) lg[j] = 0.f;
 #pragma unroll
   for (int k = 0; k < PER; ++k) o[k] = 0.f;
   for (int64_t k0 = 0; k0 < count; k0 += 32) {
@@ -286,7 +314,7 @@ __device__ __forceinline__ void merge_pieces(PtrFn ptr, int64_t c0, int64_t stri
 #pragma unroll
       for (int j = 0; j < QC; ++j) {
         w[j] = fast_exp2(__ldcg(pc + QC * D + j) - mg[j]);
-        lg[j] += __ldcg(pc + QC * D + QC + j) * w[j];
+        lg[j] = fmaf(__ldcg(pc + QC * D + QC + j), w[j], lg[j]);
       }
     } else {
 #pragma unroll
@@ -303,24 +331,23 @@ __device__ __forceinline__ void merge_pieces(PtrFn ptr, int64_t c0, int64_t stri
       for (int q = 0; q < PER; ++q) o[q] = fmaf(__ldcg(pc + lane + 32 * q), wk[(32 * q) / D], o[q]);
     }
   }
-#pragma unroll
-  for (int j = 0; j < QC; ++j)
-#pragma unroll
-    for (int off = 16; off >= 1; off >>= 1) lg[j] += __shfl_xor_sync(0xffffffffu, lg[j], off);
+  reduce_sums<QC>(lg);
 }
 
-// The same merge with every lane reading whole states, U at a time: the
-// maxima, sums and O elements of U states are all in flight together and are
-// folded in with the online log-sum-exp rule.  Needs ~24 registers per state
+// The same merge with every lane reading whole states, U at a time, so the
+// loads of U states are in flight together.  Needs ~24 registers per state
 // per lane, so it runs where the consumer's q and accumulator registers are
-// no longer live.
+// no longer live.  Each lane computes every weight itself (the same
+// fast_exp2 of the same operands as the broadcast above) and adds l_k only
+// for its own states k = lane (mod 32): bit-identical to merge_pieces.
 template <int QC, int D, int U, typename PtrFn>
 __device__ __forceinline__ void merge_pieces_wide(PtrFn ptr, int64_t c0, int64_t stride,
                                                   int64_t count, int lane, float (&o)[QC * D / 32],
                                                   float (&mg)[QC], float (&lg)[QC]) {
   constexpr int PER = QC * D / 32;
+  merge_maxima<QC, D>(ptr, c0, stride, count, lane, mg);
 #pragma unroll
-  for (int j = 0; j < QC; ++j) { mg[j] = kNegBig; lg[j] = 0.f; }
+  for (int j = 0; j < QC; ++j) lg[j] = 0.f;
 #pragma unroll
   for (int k = 0; k < PER; ++k) o[k] = 0.f;
   for (int64_t k0 = 0; k0 < count; k0 += U) {
@@ -336,28 +363,23 @@ __device__ __forceinline__ void merge_pieces_wide(PtrFn ptr, int64_t c0, int64_t
         }
 #pragma unroll
         for (int q = 0; q < PER; ++q) os[u][q] = __ldcg(pc + lane + 32 * q);
-      } else {
-#pragma unroll
-        for (int j = 0; j < QC; ++j) { ms[u][j] = kNegBig; ls[u][j] = 0.f; }
-#pragma unroll
-        for (int q = 0; q < PER; ++q) os[u][q] = 0.f;
       }
     }
 #pragma unroll
     for (int u = 0; u < U; ++u) {
-      float a[QC], b[QC];
+      if (k0 + u < count) {
+        float w[QC];
 #pragma unroll
-      for (int j = 0; j < QC; ++j) {
-        const float mn = fmaxf(mg[j], ms[u][j]);
-        a[j] = fast_exp2(mg[j] - mn);
-        b[j] = fast_exp2(ms[u][j] - mn);
-        lg[j] = lg[j] * a[j] + ls[u][j] * b[j];
-        mg[j] = mn;
+        for (int j = 0; j < QC; ++j) {
+          w[j] = fast_exp2(ms[u][j] - mg[j]);
+          if ((int)((k0 + u) & 31) == lane) lg[j] = fmaf(ls[u][j], w[j], lg[j]);
+        }
+#pragma unroll
+        for (int q = 0; q < PER; ++q) o[q] = fmaf(os[u][q], w[(32 * q) / D], o[q]);
       }
-#pragma unroll
-      for (int q = 0; q < PER; ++q) o[q] = o[q] * a[(32 * q) / D] + os[u][q] * b[(32 * q) / D];
     }
   }
+  reduce_sums<QC>(lg);
 }
 
 template <typename T, int D, int QC>
@@ -700,8 +722,21 @@ __global__ void __launch_bounds__(Limits<T, D, QC>::THREADS, 1)
       __threadfence();
       __syncwarp();
       int old = 0;
-      if (lane == 0) old = epoch_arrive(counter, p.epoch);
+      if (lane == 0) old = epoch_arrive(counter, p.epoch, p.arrive_rounds);
       return __shfl_sync(0xffffffffu, old, 0);
+    };
+    // An arrival that never registered leaves its merge incomplete for every
+    // warp, so this warp owns the rows: NaN, and the error bit.
+    auto give_up = [&]() {
+      constexpr int PERG = QC * D / 32;
+#pragma unroll
+      for (int k = 0; k < PERG; ++k) {
+        const int j = (32 * k) / D;
+        const int e = (lane + 32 * k) - j * D;
+        p.out[((int64_t)pb * p.H + phead0 + j) * D + e] = __int_as_float(0x7fc00000);
+      }
+      if (p.lse && lane < QC) p.lse[(int64_t)pb * p.H + phead0 + lane] = __int_as_float(0x7fc00000);
+      if (lane == 0) report(p.dev_status, PA_DEVERR_MERGE);
     };
     constexpr int PER = QC * D / 32;
     float o[PER], mg[QC], lg[QC];
@@ -711,7 +746,12 @@ __global__ void __launch_bounds__(Limits<T, D, QC>::THREADS, 1)
       const int64_t g0 = first + ((cta - first) / kGroup) * kGroup;
       const int64_t g1 = g0 + kGroup - 1 < last ? g0 + kGroup - 1 : last;
       const int o2 = (g0 == first && first_late) ? 1 : 0;
-      go = arrive(&p.grp_counters[(g0 * 2 + o2) * NS + slot]) == (int)(g1 - g0);
+      const int got = arrive(&p.grp_counters[(g0 * 2 + o2) * NS + slot]);
+      if (got < 0) {
+        give_up();
+        return;
+      }
+      go = got == (int)(g1 - g0);
       if (go) {
         __threadfence();
         if (wide) merge_pieces_wide<QC, D, 4>(piece, g0, 1, g1 - g0 + 1, lane, o, mg, lg);
@@ -729,7 +769,13 @@ __global__ void __launch_bounds__(Limits<T, D, QC>::THREADS, 1)
       n_top = (npieces + kGroup - 1) / kGroup;
       top_stride = kGroup;
     }
-    if (go && arrive(&p.counters[((int64_t)pgc * p.B + pb) * NS + slot]) == (int)(n_top - 1)) {
+    if (!go) return;
+    const int got_top = arrive(&p.counters[((int64_t)pgc * p.B + pb) * NS + slot]);
+    if (got_top < 0) {
+      give_up();
+      return;
+    }
+    if (got_top == (int)(n_top - 1)) {
       __threadfence();
       if (wide) merge_pieces_wide<QC, D, 4>(piece, first, top_stride, n_top, lane, o, mg, lg);
       else merge_pieces<QC, D>(piece, first, top_stride, n_top, lane, o, mg, lg);

@@ -17,13 +17,18 @@
 // stand-in, not a device address), so on the first call on each device -- with
 // that device current -- the library asks the runtime for the array's device
 // address with cudaGetSymbolAddress and caches it.  That first call on a device
-// should therefore come before any stream capture.  Every call on a device
-// shares the one array and leaves its contents behind; the plan kernel of each
-// call rewrites the tables and zeroes the counters it needs, so no state leaks
-// from one call into the next -- but two calls whose work overlaps on the GPU
-// (different streams, or different host threads) race on the array, so callers
-// must order them.  Requests that need more scratch than the array holds are
-// rejected with PA_ERR_TOO_LARGE before anything is launched.
+// should therefore come before any stream capture.  The cached address belongs
+// to the device's context of that moment: cudaDeviceReset destroys it, so the
+// entry point must not be used across a reset of the device in the same
+// process.  Every call on a device shares the one array and leaves its
+// contents behind.  Nothing from one call reaches the next: the merge counters
+// and the abort flag carry a tag of the launch that wrote them (a new tag per
+// launch), so values left by an earlier call read as zero, and the plan tables
+// are rebuilt by every call (in shared memory for up to 1024 sequences, by the
+// plan kernel into the array above that).  Two calls whose work overlaps on
+// the GPU (different streams, or different host threads) race on the array,
+// so callers must order them.  Requests that need more scratch than the array
+// holds are rejected with PA_ERR_TOO_LARGE before anything is launched.
 #include <mutex>
 #include <utility>
 #include <vector>

@@ -26,7 +26,7 @@ PA_ERR_WORKSPACE = 7
 PA_ERR_CUDA = 8
 PA_ERR_TOO_LARGE = 9
 PA_ERR_NO_DEVICE = 10
-PA_DEVERR_BLOCK_ID, PA_DEVERR_CONTEXT, PA_DEVERR_TIMEOUT = 1, 2, 4
+PA_DEVERR_BLOCK_ID, PA_DEVERR_CONTEXT, PA_DEVERR_TIMEOUT, PA_DEVERR_MERGE = 1, 2, 4, 8
 PA_IPC_HANDLE_BYTES = 64
 
 _P = ctypes.c_void_p
@@ -41,6 +41,7 @@ SIGNATURES = {
     "pa_abi_version": (_I, []),
     "pa_strerror": (ctypes.c_char_p, [_I]),
     "pa_last_cuda_error": (_I, []),
+    "pa_set_merge_arrive_rounds": (_I, [_I]),
     "pa_choose_num_splits": (_I64, [_I64, _I64, _I64]),
     "pa_decode_workspace_size": (_I, [_I64, _I64, _I64, _I64, _I, _I64, _I64, _I64,
                                       ctypes.POINTER(_SZ)]),

@@ -85,8 +85,20 @@ typedef enum pa_status {
 #define PA_DEVERR_BLOCK_ID 0x1   /* block id outside [0, num_blocks)          */
 #define PA_DEVERR_CONTEXT 0x2    /* context_lens[b] > max_blocks * block_size */
 #define PA_DEVERR_TIMEOUT 0x4    /* a bounded pipeline wait gave up           */
+#define PA_DEVERR_MERGE 0x8      /* a split-merge arrival never registered;
+                                    its rows are NaN                           */
 
 PA_API int pa_abi_version(void);
+
+/* Failure-path test hook, no counterpart in the reference.  Sets the number
+ * of compare-and-swap rounds a decode CTA spends registering its split piece
+ * with the merge counter before it gives up (default 1 << 20, never reached
+ * in practice).  A give-up writes NaN into the rows of that piece and ORs
+ * PA_DEVERR_MERGE into *dev_status; 0 makes every arrival give up, which lets
+ * a test drive that path without a fault or a hang.  `rounds` < 0 restores
+ * the default.  Process-wide; applies to launches made after the call.
+ * Returns the previous value. */
+PA_API int pa_set_merge_arrive_rounds(int rounds);
 PA_API const char* pa_strerror(int status);
 /* cudaError_t of the most recent PA_ERR_CUDA on this thread (0 if none) */
 PA_API int pa_last_cuda_error(void);
@@ -174,8 +186,10 @@ PA_API int pa_paged_attention_v2(float* out, const float* q, const void* k_cache
  * the library until exit); sizes whose pa_decode_workspace_size exceeds it
  * return PA_ERR_TOO_LARGE without launching.  The first call on a device
  * looks up the array's device address (cudaGetSymbolAddress) with that device
- * current; make that first call before any stream capture.  All calls on a
- * device share the array, so calls that overlap on the GPU race: order them.
+ * current; make that first call before any stream capture.  The address is
+ * kept for the life of the process: do not use this entry point across a
+ * cudaDeviceReset of the device.  All calls on a device share the array, so
+ * calls that overlap on the GPU race: order them.
  * Calls no cudaMalloc / cudaFree and no allocating library routine. */
 #define PA_NOALLOC_SCRATCH_BYTES (8u << 20)
 PA_API int pa_paged_attention_v3_noalloc(

@@ -2,8 +2,9 @@
 
 TEST INFRASTRUCTURE ONLY (the checker, never the product).  Nothing is copied:
 the compilers read the files where they lie under the reference checkout
-(default /root/reference, or $GB10_REF).  Outputs go to oracle/_ref/ only
-(git-ignored; it travels to the GPU box with the tree).
+($GB10_REF, else a checkout named ``reference`` beside this repository).
+Outputs go to oracle/_ref/ only (git-ignored; it travels to the GPU box with
+the tree).
 
 * libref_arm_scalar.so -- gb10-attn arm_cpu/src/scalar.cpp (the reference's
   scalar dot / scores / softmax lane) + ref_arm_shim.cpp, with the reference's
@@ -13,6 +14,11 @@ the compilers read the files where they lie under the reference checkout
   kernels/paged_attn_v3.h:5-7) for -gencode arch=compute_100a,code=sm_100a,
   + ref_kernels_bind.cpp.  Runs only on a GPU; used by -m gpu tests and by
   tests/golden/make_golden.py.
+* arm_attn_bench -- the reference's own CPU microbenchmark
+  (arm_cpu/src/{bench,scalar,neon,sve,features}.cpp, flags of
+  arm_cpu/CMakeLists.txt: -O3, -fno-tree-vectorize on scalar.cpp).  bench.py's
+  CPU-baseline leg runs ``--backend scalar --tokens 2048 --dim 64`` (scores +
+  softmax of one head, no V, no paging) beside the scalar decode restatement.
 
 The reference's only full CPU paged decode (cpu_reference in
 rocm/hip/paged_attn_v1_hip.cpp) sits in a HIP translation unit that needs the
@@ -29,7 +35,7 @@ from pathlib import Path
 
 HERE = Path(__file__).resolve().parent
 OUT = HERE / "_ref"
-REF = Path(os.environ.get("GB10_REF", "/root/reference"))
+REF = Path(os.environ.get("GB10_REF", str(HERE.parent.parent / "reference")))
 KERNELS = ["paged_attn_v1", "paged_attn_v2", "paged_attn_v3", "paged_attn_prefill",
            "paged_attn_wmma"]
 
@@ -54,6 +60,27 @@ def build_arm_scalar(force: bool = False) -> Path:
     _run(["g++", "-O3", "-std=c++20", "-fno-tree-vectorize", "-fPIC", "-shared",
           f"-I{REF / 'arm_cpu' / 'include'}", str(src), str(HERE / "ref_arm_shim.cpp"),
           "-o", str(out)])
+    return out
+
+
+def build_arm_bench(force: bool = False) -> Path:
+    out = OUT / "arm_attn_bench"
+    if out.exists() and not force:
+        return out
+    OUT.mkdir(exist_ok=True)
+    obj_dir = OUT / "obj_arm"
+    obj_dir.mkdir(exist_ok=True)
+    src = REF / "arm_cpu" / "src"
+    objs = []
+    for name in ("bench", "scalar", "neon", "sve", "features"):
+        o = obj_dir / f"{name}.o"
+        extra = ["-fno-tree-vectorize"] if name == "scalar" else []
+        _run(["g++", "-O3", "-std=c++20", *extra, f"-I{REF / 'arm_cpu' / 'include'}",
+              "-c", str(src / f"{name}.cpp"), "-o", str(o)])
+        objs.append(o)
+    _run(["g++", "-o", str(out), *map(str, objs)])
+    for o in objs:
+        o.unlink(missing_ok=True)
     return out
 
 
@@ -103,6 +130,7 @@ def build(force: bool = False) -> bool:
     if not available():
         return False
     build_arm_scalar(force)
+    build_arm_bench(force)
     build_cuda_kernels(force)
     return True
 

@@ -43,3 +43,16 @@ def test_reference_arm_other_ranks_are_silent():
                   env={"RANK": "1", "LOCAL_RANK": "1", "WORLD_SIZE": "2"})
     assert r.returncode == 0
     assert not [ln for ln in r.stdout.splitlines() if ln.startswith("{")]
+
+
+def test_failing_rank_prints_a_json_error_line():
+    # the B200 arm on a host without a usable GPU fails early: the failing
+    # rank names itself and its phase on stdout, and exits non-zero
+    r = run_bench("--steps", "1", "--warmup", "1", "--no-e2e", "--no-extra",
+                  "--no-cpu-baseline", env={"CUDA_VISIBLE_DEVICES": "", "RANK": "3",
+                                            "LOCAL_RANK": "0", "WORLD_SIZE": "1"})
+    assert r.returncode != 0
+    lines = [ln for ln in r.stdout.splitlines() if ln.startswith("{")]
+    assert lines, r.stdout[-2000:] + r.stderr[-2000:]
+    err = json.loads(lines[-1])
+    assert err["rank"] == 3 and err["where"] and err["error"] and err["impl"] == "b200"

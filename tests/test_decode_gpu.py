@@ -241,7 +241,8 @@ def test_validate_block_tables():
 
 
 def test_repeated_calls_reuse_workspace_state():
-    # the merge counters are re-zeroed by each call's plan kernel
+    # one workspace reused call after call: the merge counters carry each
+    # launch's tag, so what an earlier call left reads as zero
     q, k, v, bt, ctx = case(21, 2, 8, 8, 64, 16, [3000, 5000], "float16")
     ref = orc.decode(q, k, v, bt, ctx, 0.125, threads=8)
     for _ in range(3):

@@ -5,8 +5,10 @@ memory up front).  Its scratch lives in a fixed 8 MiB array inside the library.
 
 Checked through the C ABI against the regular entry point (which takes a
 caller-allocated workspace), within the decode tolerance of the other tests
-(max-abs 2e-3), on two calls in a row with different inputs -- the array keeps
-the previous call's contents, so the second call shows nothing stale leaks.
+(max-abs 2e-3), on calls in a row with different inputs -- the array keeps
+the previous call's contents, so the later calls show nothing stale leaks.
+The third case has more than 1024 sequences, where the plan tables themselves
+live in the array.
 Named to be collected last; it passes alone in a fresh process as well."""
 from __future__ import annotations
 
@@ -46,10 +48,19 @@ def test_noalloc_matches_workspace_entry_point_two_calls_in_a_row():
         (orc.make_decode_case(71, 4, 32, 8, 128, 16, [5000, 17, 1200, 300]), "bfloat16", 128),
         # gpt2 geometry, fp16, different sizes for the second call
         (orc.make_decode_case(72, 16, 12, 12, 64, 16, 2048), "float16", 64),
+        # more than 1024 short sequences: the plan kernel writes its tables
+        # into the library's array (smaller batches plan in shared memory)
+        (orc.make_decode_case(73, 1100, 12, 12, 64, 16,
+                              np.random.default_rng(73).integers(1, 80, 1100)), "float16", 64),
     ]
     for (q, k, v, bt, ctx), dtype, D in cases:
         k, v = orc.round_to(k, dtype), orc.round_to(v, dtype)
         scale = D ** -0.5
+        n = ctypes.c_size_t(0)
+        _lib.check("ws", _lib.call("pa_decode_workspace_size", q.shape[0], q.shape[1],
+                                   k.shape[2], D, PA_DT[dtype], 16, bt.shape[1], 0,
+                                   ctypes.byref(n)))
+        assert n.value <= LIMIT
         ref_out, ref_lse = abi_decode(q, k, v, bt, ctx, scale, dtype, want_lse=True)
         out, lse = noalloc_decode(q, k, v, bt, ctx, scale, dtype)
         assert max_abs(out, ref_out) <= 2e-3
