@@ -40,7 +40,7 @@ NVCC_FLAGS = ARCH + ["-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC",
 
 CU_SOURCES = ["abi.cu", "decode.cu", "decode_f16.cu", "decode_bf16.cu", "decode_f32.cu",
               "decode_f64.cu", "decode_e4m3.cu", "decode_static.cu", "write_kv.cu",
-              "prefill.cu", "prefill_tc.cu", "peer_merge.cu"]
+              "prefill.cu", "prefill_tc.cu", "prefill_pair.cu", "peer_merge.cu"]
 LIB = OUT_DIR / "libpa_b200.so"
 SHIM = OUT_DIR / "_pa_b200_torch.so"
 

@@ -191,6 +191,37 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity,
   }
 }
 
+// The same bounded wait with acquire at cluster scope: for barriers that
+// threads of another CTA of the cluster arrive on (their release.cluster
+// arrivals then order their earlier writes before this thread's later reads).
+__device__ __forceinline__ bool mbar_try_wait_cl(uint64_t* bar, uint32_t parity, uint32_t hint_ns) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity), "r"(hint_ns)
+      : "memory");
+  return ok != 0;
+}
+
+__device__ __forceinline__ bool mbar_wait_cl(uint64_t* bar, uint32_t parity, int32_t* abort_flag,
+                                             int32_t abort_tag = 1) {
+  if (mbar_try_wait_cl(bar, parity, 0u)) return true;
+  const uint64_t t0 = globaltimer_ns();
+  for (uint32_t it = 1;; ++it) {
+    if (mbar_try_wait_cl(bar, parity, 100000u)) return true;
+    if ((it & 7) == 0) {
+      if (abort_flag && *reinterpret_cast<volatile int32_t*>(abort_flag) == abort_tag) return false;
+      if (globaltimer_ns() - t0 > kWaitLimitNs) {
+        if (abort_flag) atomicExch(abort_flag, abort_tag);
+        return false;
+      }
+    }
+  }
+}
+
 // 1-D bulk async copy global -> shared (TMA engine), completing on `bar`.
 // dst, src and bytes must be multiples of 16; dst is this CTA's own shared memory.
 __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes,

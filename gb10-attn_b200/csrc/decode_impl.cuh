@@ -262,124 +262,83 @@ __device__ __forceinline__ void fused_plan(const Params& p, int32_t* tile_off_s,
 
 // Log-sum-exp merge of the partial states at ptr(c0), ptr(c0 + stride), ...
 // (count of them; layout [QC][D] un-normalised O, then QC maxima, then QC
-// sums).  One warp.  The result is a fixed function of the states: the
-// maxima first (exact), then every state's weight w_k = 2^(m_k - mg) and
-// o += O_k * w_k by fmaf in state order, and l summed per lane over states
-// k = lane, lane + 32, ... before one xor-tree reduction.  Both variants below
-// follow exactly that order, so whichever warp happens to merge a sequence
-// (the last to arrive, which varies from launch to launch) writes the same
-// bits.  Every lane ends with the merged maxima mg, sums lg and elements
-// lane + 32k of O in o[k].
-template <int QC, int D, typename PtrFn>
-__device__ __forceinline__ void merge_maxima(PtrFn ptr, int64_t c0, int64_t stride, int64_t count,
-                                             int lane, float (&mg)[QC]) {
+// sums).  One warp.  The result is a fixed function of the states: they are
+// folded in state order with the online rule (fold_state, every operation
+// pinned by fmaf / __fmul_rn), so whichever warp merges a sequence (the last
+// to arrive, which varies from launch to launch) writes the same bits.
+// Every lane ends with the merged maxima mg, sums lg and elements lane + 32k
+// of O in o[k].
+template <int QC, int D>
+__device__ __forceinline__ void fold_state(float (&o)[QC * D / 32], float (&mg)[QC],
+                                           float (&lg)[QC], const float (&ms)[QC],
+                                           const float (&ls)[QC], const float (&os)[QC * D / 32]) {
+  constexpr int PER = QC * D / 32;
+  float a[QC], b[QC];
 #pragma unroll
-  for (int j = 0; j < QC; ++j) mg[j] = kNegBig;
-  for (int64_t k = lane; k < count; k += 32) {
-    const float* pc = ptr(c0 + k * stride);
-#pragma unroll
-    for (int j = 0; j < QC; ++j) mg[j] = fmaxf(mg[j], __ldcg(pc + QC * D + j));
+  for (int j = 0; j < QC; ++j) {
+    const float mn = fmaxf(mg[j], ms[j]);
+    a[j] = fast_exp2(mg[j] - mn);
+    b[j] = fast_exp2(ms[j] - mn);
+    lg[j] = fmaf(ls[j], b[j], __fmul_rn(lg[j], a[j]));
+    mg[j] = mn;
   }
 #pragma unroll
-  for (int j = 0; j < QC; ++j)
-#pragma unroll
-    for (int off = 16; off >= 1; off >>= 1) mg[j] = fmaxf(mg[j], __shfl_xor_sync(0xffffffffu, mg[j], off));
+  for (int q = 0; q < PER; ++q)
+    o[q] = fmaf(os[q], b[(32 * q) / D], __fmul_rn(o[q], a[(32 * q) / D]));
 }
 
-template <int QC>
-__device__ __forceinline__ void reduce_sums(float (&lg)[QC]) {
+template <int QC, int D, typename PtrFn>
+__device__ __forceinline__ void load_state(PtrFn ptr, int64_t c, int lane, float (&ms)[QC],
+                                           float (&ls)[QC], float (&os)[QC * D / 32]) {
+  const float* pc = ptr(c);
 #pragma unroll
-  for (int j = 0; j < QC; ++j)
+  for (int j = 0; j < QC; ++j) {
+    ms[j] = __ldcg(pc + QC * D + j);
+    ls[j] = __ldcg(pc + QC * D + QC + j);
+  }
 #pragma unroll
-    for (int off = 16; off >= 1; off >>= 1) lg[j] += __shfl_xor_sync(0xffffffffu, lg[j], off);
+  for (int q = 0; q < QC * D / 32; ++q) os[q] = __ldcg(pc + lane + 32 * q);
 }
 
-// Lane k computes the weights of states k, k + 32, ... and broadcasts them;
-// the O rows are read one state at a time (few registers: usable inside the
-// consumer loop).
+// One state at a time (few registers: usable inside the consumer loop).
 template <int QC, int D, typename PtrFn>
 __device__ __forceinline__ void merge_pieces(PtrFn ptr, int64_t c0, int64_t stride, int64_t count,
                                              int lane, float (&o)[QC * D / 32], float (&mg)[QC],
                                              float (&lg)[QC]) {
   constexpr int PER = QC * D / 32;
-  merge_maxima<QC, D>(ptr, c0, stride, count, lane, mg);
 #pragma unroll
-  for (int j = 0; j < QC; ++j) lg[j] = 0.f;
+  for (int j = 0; j < QC; ++j) { mg[j] = kNegBig; lg[j] = 0.f; }
 #pragma unroll
   for (int k = 0; k < PER; ++k) o[k] = 0.f;
-  for (int64_t k0 = 0; k0 < count; k0 += 32) {
-    float w[QC];
-    if (k0 + lane < count) {
-      const float* pc = ptr(c0 + (k0 + lane) * stride);
-#pragma unroll
-      for (int j = 0; j < QC; ++j) {
-        w[j] = fast_exp2(__ldcg(pc + QC * D + j) - mg[j]);
-        lg[j] = fmaf(__ldcg(pc + QC * D + QC + j), w[j], lg[j]);
-      }
-    } else {
-#pragma unroll
-      for (int j = 0; j < QC; ++j) w[j] = 0.f;
-    }
-    const int nthis = (int)(count - k0 < 32 ? count - k0 : 32);
-#pragma unroll 4
-    for (int k = 0; k < nthis; ++k) {
-      const float* pc = ptr(c0 + (k0 + k) * stride);
-      float wk[QC];
-#pragma unroll
-      for (int j = 0; j < QC; ++j) wk[j] = __shfl_sync(0xffffffffu, w[j], k);
-#pragma unroll
-      for (int q = 0; q < PER; ++q) o[q] = fmaf(__ldcg(pc + lane + 32 * q), wk[(32 * q) / D], o[q]);
-    }
+#pragma unroll 2
+  for (int64_t k = 0; k < count; ++k) {
+    float ms[QC], ls[QC], os[PER];
+    load_state<QC, D>(ptr, c0 + k * stride, lane, ms, ls, os);
+    fold_state<QC, D>(o, mg, lg, ms, ls, os);
   }
-  reduce_sums<QC>(lg);
 }
 
-// The same merge with every lane reading whole states, U at a time, so the
-// loads of U states are in flight together.  Needs ~24 registers per state
-// per lane, so it runs where the consumer's q and accumulator registers are
-// no longer live.  Each lane computes every weight itself (the same
-// fast_exp2 of the same operands as the broadcast above) and adds l_k only
-// for its own states k = lane (mod 32): bit-identical to merge_pieces.
+// The same merge with U states' loads in flight together (~24 registers per
+// state per lane: runs where the consumer's q and accumulator registers are
+// no longer live).  Same fold, same order: bit-identical to merge_pieces.
 template <int QC, int D, int U, typename PtrFn>
 __device__ __forceinline__ void merge_pieces_wide(PtrFn ptr, int64_t c0, int64_t stride,
                                                   int64_t count, int lane, float (&o)[QC * D / 32],
                                                   float (&mg)[QC], float (&lg)[QC]) {
   constexpr int PER = QC * D / 32;
-  merge_maxima<QC, D>(ptr, c0, stride, count, lane, mg);
 #pragma unroll
-  for (int j = 0; j < QC; ++j) lg[j] = 0.f;
+  for (int j = 0; j < QC; ++j) { mg[j] = kNegBig; lg[j] = 0.f; }
 #pragma unroll
   for (int k = 0; k < PER; ++k) o[k] = 0.f;
   for (int64_t k0 = 0; k0 < count; k0 += U) {
     float ms[U][QC], ls[U][QC], os[U][PER];
 #pragma unroll
-    for (int u = 0; u < U; ++u) {
-      if (k0 + u < count) {
-        const float* pc = ptr(c0 + (k0 + u) * stride);
+    for (int u = 0; u < U; ++u)
+      if (k0 + u < count) load_state<QC, D>(ptr, c0 + (k0 + u) * stride, lane, ms[u], ls[u], os[u]);
 #pragma unroll
-        for (int j = 0; j < QC; ++j) {
-          ms[u][j] = __ldcg(pc + QC * D + j);
-          ls[u][j] = __ldcg(pc + QC * D + QC + j);
-        }
-#pragma unroll
-        for (int q = 0; q < PER; ++q) os[u][q] = __ldcg(pc + lane + 32 * q);
-      }
-    }
-#pragma unroll
-    for (int u = 0; u < U; ++u) {
-      if (k0 + u < count) {
-        float w[QC];
-#pragma unroll
-        for (int j = 0; j < QC; ++j) {
-          w[j] = fast_exp2(ms[u][j] - mg[j]);
-          if ((int)((k0 + u) & 31) == lane) lg[j] = fmaf(ls[u][j], w[j], lg[j]);
-        }
-#pragma unroll
-        for (int q = 0; q < PER; ++q) o[q] = fmaf(os[u][q], w[(32 * q) / D], o[q]);
-      }
-    }
+    for (int u = 0; u < U; ++u)
+      if (k0 + u < count) fold_state<QC, D>(o, mg, lg, ms[u], ls[u], os[u]);
   }
-  reduce_sums<QC>(lg);
 }
 
 template <typename T, int D, int QC>

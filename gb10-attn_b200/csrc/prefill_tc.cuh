@@ -1,0 +1,464 @@
+// prefill_tc.cuh -- pieces shared by the tensor-core prefill kernels
+// (prefill_tc.cu: one CTA per 128 query rows; prefill_pair.cu: a CTA pair
+// sharing one M = 256 MMA): launch parameters, tile constants, the Q / P
+// operand packing, the 128-byte swizzle and the warp-uniform bounded wait.
+#pragma once
+
+#include <cudaTypedefs.h>
+
+#include "common.cuh"
+#include "tcgen05.cuh"
+
+namespace pa {
+namespace prefill {
+
+constexpr int BM = 128;  // query rows per CTA
+constexpr int BN = 128;  // keys per KV tile
+// Warpgroups 0-1: softmax (warpgroup g takes the KV tiles j % 2 == g);
+// warpgroup 2: warp 8 issues the MMAs, warp 9 the TMA loads, warps 10-11 idle.
+// Registers: 384 threads launched at 168 (64512); setmaxnreg gives the
+// softmax warpgroups 232 and the rest 40: 256 x 232 + 128 x 40 = 64512.
+constexpr int kSoftmaxWarps = 8;
+constexpr int kMmaWarp = 8;
+constexpr int kTmaWarp = 9;
+constexpr int kThreads = 384;
+constexpr int kSoftmaxRegs = 232, kOtherRegs = 40;
+static_assert(256 * kSoftmaxRegs + 128 * kOtherRegs <= kThreads * 168, "register split");
+constexpr uint32_t kTmemCols = 512;
+// block ids the TMA warp stages in shared memory per refill (32 tiles at 16-token pages)
+constexpr int kBtChunk = 256;
+
+struct Params {
+  CUtensorMap tmap_k;  // 3-D [D, HKV, NB*BS] views of the pool, box {64, 1, 16}
+  CUtensorMap tmap_v;
+  float* out;                    // [B, Sq, H, D]
+  const float* q;                // [B, Sq, H, D]
+  const char* v_pool;            // [NB, BS, HKV, D] (rows past the context: sanitised copies)
+  const int32_t* block_tables;   // [B, MB]
+  const int32_t* context_lens;   // [B]
+  int32_t* dev_status;
+  int64_t B, Sq, H, HKV, MB, NB, BS;
+  int32_t n_qtiles;
+  float qscale;                  // scale * log2(e)
+};
+
+template <typename T>
+struct Fmt;
+template <> struct Fmt<__nv_bfloat16> { static constexpr int id = 1; static constexpr bool split = true; };
+template <> struct Fmt<__half> { static constexpr int id = 0; static constexpr bool split = false; };
+
+template <typename T, int D>
+struct Cfg {
+  static constexpr bool SPLIT = Fmt<T>::split;
+  static constexpr int NH = D / 64;                 // 64-element (128-byte) column halves
+  static constexpr uint32_t Q_BYTES = BM * D * 2;   // one Q part
+  static constexpr uint32_t KV_BYTES = BN * D * 2;  // K or V of one tile
+  // K stages are freed as soon as S = Q K^T is done, V stages after P V, so
+  // the K ring runs one tile deeper.
+  static constexpr int NK = D == 128 ? 3 : 4;
+  static constexpr int NV = D == 128 ? 2 : 4;
+  static constexpr uint32_t OFF_QH = 0;
+  static constexpr uint32_t OFF_QL = Q_BYTES;
+  static constexpr uint32_t OFF_K = Q_BYTES * (SPLIT ? 2 : 1);
+  static constexpr uint32_t OFF_V = OFF_K + NK * KV_BYTES;
+  static constexpr uint32_t OFF_BAR = OFF_V + NV * KV_BYTES;
+  // mbarriers: K and V full/empty rings, s_full/p_full/o_ready pairs, q_ready,
+  // 4 pair barriers; then the TMEM address and the abort flag
+  static constexpr uint32_t N_BARS = 2 * NK + 2 * NV + 2 * 3 + 1 + 4;
+  static constexpr uint32_t OFF_BT = OFF_BAR + ((N_BARS * 8 + 8 + 15) / 16) * 16;
+  static constexpr uint32_t SMEM = OFF_BT + kBtChunk * 4 + 1024;  // + alignment slack
+  static_assert(SMEM <= 227 * 1024, "shared memory budget");
+  // TMEM columns: S buffers at 0 and 128 (tiles j % 2), O of the two
+  // softmax warpgroups at 256 and 256 + D
+  static constexpr uint32_t COL_S0 = 0, COL_S1 = 128, COL_O = 256;
+};
+
+__device__ __forceinline__ uint32_t pack2(float lo, float hi, __nv_bfloat16*) {
+  uint32_t r;
+  asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
+  return r;
+}
+__device__ __forceinline__ uint32_t pack2(float lo, float hi, __half*) {
+  uint32_t r;
+  asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
+  return r;
+}
+__device__ __forceinline__ float unpack_lo(uint32_t u, __nv_bfloat16*) { return __uint_as_float(u << 16); }
+__device__ __forceinline__ float unpack_hi(uint32_t u, __nv_bfloat16*) { return __uint_as_float(u & 0xffff0000u); }
+__device__ __forceinline__ float unpack_lo(uint32_t u, __half*) {
+  return __half2float(__ushort_as_half((unsigned short)(u & 0xffffu)));
+}
+__device__ __forceinline__ float unpack_hi(uint32_t u, __half*) {
+  return __half2float(__ushort_as_half((unsigned short)(u >> 16)));
+}
+
+// Two fp32 values -> packed 16-bit pair (first value in the low half).  For
+// bf16 also the remainder pair: hi = the fp32 bits truncated to bf16 (exact),
+// lo = round-to-nearest bf16 of the exact fp32 remainder x - hi, so hi + lo
+// carries x to ~2^-16 relative.  fp16: one round-to-nearest pair, lo unused.
+__device__ __forceinline__ void split_pair(float a, float b, uint32_t& hi, uint32_t& lo,
+                                           __nv_bfloat16*) {
+  const uint32_t ua = __float_as_uint(a), ub = __float_as_uint(b);
+  hi = __byte_perm(ua, ub, 0x7632);
+  const float ra = a - __uint_as_float(ua & 0xffff0000u);
+  const float rb = b - __uint_as_float(ub & 0xffff0000u);
+  lo = pack2(ra, rb, (__nv_bfloat16*)nullptr);
+}
+__device__ __forceinline__ void split_pair(float a, float b, uint32_t& hi, uint32_t& lo, __half*) {
+  hi = pack2(a, b, (__half*)nullptr);
+  lo = 0;
+}
+
+// Softmax weights (p0, p1) of two adjacent keys -> the MMA operand pair(s).
+// bf16: hi = the fp32 bits truncated to bf16, lo = the remainder p - hi
+// (exact in fp32) truncated to bf16; hi + lo carries p to 2^-16 relative,
+// with integer byte permutes instead of conversions.  fp16: one
+// round-to-nearest pair.
+__device__ __forceinline__ void p_pair(float p0, float p1, uint32_t& hi, uint32_t& lo,
+                                       __nv_bfloat16*) {
+  const uint32_t a = __float_as_uint(p0), b = __float_as_uint(p1);
+  hi = __byte_perm(a, b, 0x7632);
+  const float2 r = fma2(make_float2(__uint_as_float(a & 0xffff0000u), __uint_as_float(b & 0xffff0000u)),
+                        make_float2(-1.f, -1.f), make_float2(p0, p1));
+  lo = __byte_perm(__float_as_uint(r.x), __float_as_uint(r.y), 0x7632);
+}
+__device__ __forceinline__ void p_pair(float p0, float p1, uint32_t& hi, uint32_t& lo, __half*) {
+  hi = pack2(p0, p1, (__half*)nullptr);
+  lo = 0;
+}
+
+// Byte offset of element (r, k) of a [rows x D] K-major tile stored as D/64
+// swizzled 128-byte-row halves of `rows * 128` bytes each (the layout the
+// tensor core reads with a SWIZZLE_128B descriptor, and TMA writes).
+__device__ __forceinline__ uint32_t sw128_offset(int r, int k, int rows) {
+  const int half = k >> 6, kk = k & 63, chunk = kk >> 3;
+  return (uint32_t)(half * rows * 128 + (r >> 3) * 1024 + (r & 7) * 128 +
+                    ((chunk ^ (r & 7)) << 4) + (kk & 7) * 2);
+}
+
+// One lane writes one 16-token group x 64-column half of a V tile (the
+// 128-byte-swizzled layout TMA produces) for a group that reaches past the
+// context: tokens < ctx are copied from the pool rows `row0 + i` (16-byte
+// loads), the rest are zeros, so no P = 0 weight meets a NaN or Inf of an
+// unwritten pool row.  `dst` is the group's first row in the stage.
+__device__ __forceinline__ void v_group_sanitised(unsigned char* dst, const char* v_pool,
+                                                  int64_t row0, int64_t valid, int64_t HKV,
+                                                  int64_t kv_h, int hf, int64_t D) {
+#pragma unroll 1
+  for (int i = 0; i < 16; ++i) {
+    const uint4* src = reinterpret_cast<const uint4*>(
+        v_pool + (((row0 + i) * HKV + kv_h) * D + hf * 64) * 2);
+    unsigned char* drow = dst + (i >> 3) * 1024 + (i & 7) * 128;  // group rows start 8-aligned
+#pragma unroll
+    for (int c = 0; c < 8; ++c) {
+      const uint4 v = i < valid ? __ldg(src + c) : make_uint4(0, 0, 0, 0);
+      *reinterpret_cast<uint4*>(drow + ((c ^ (i & 7)) << 4)) = v;
+    }
+  }
+}
+
+// Warp-uniform bounded wait: lane 0 waits, the verdict is broadcast, then
+// every lane observes the completed phase itself (acquire).  The warp never
+// diverges around the .sync.aligned tcgen05 loads / stores that follow.
+__device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, int32_t* abort_flag) {
+  int ok = 1;
+  if ((threadIdx.x & 31) == 0) ok = mbar_wait(bar, parity, abort_flag) ? 1 : 0;
+  ok = __shfl_sync(0xffffffffu, ok, 0);
+  if (ok) (void)mbar_wait(bar, parity, abort_flag);
+  return ok != 0;
+}
+
+// Barriers the softmax warps use (this CTA's shared memory).
+struct Bars {
+  uint64_t* s_full;    // [2] S tile of group g in tensor memory (MMA commit)
+  uint64_t* p_full;    // [2] P of group g written (softmax arrivals; the leader's in a pair)
+  uint64_t* o_ready;   // [2] P V of group g done (MMA commit)
+  uint64_t* q_ready;   // Q staged (softmax arrivals; the leader's in a pair)
+  uint64_t* pair_bar;  // [4] (m, l) exchange of a warp pair
+};
+
+// Warp-uniform bounded wait; CL: acquire at cluster scope (barriers another
+// CTA of the pair arrives on or commits to).
+template <bool CL>
+__device__ __forceinline__ bool warp_wait_t(uint64_t* bar, uint32_t parity, int32_t* abort_flag) {
+  int ok = 1;
+  if ((threadIdx.x & 31) == 0)
+    ok = (CL ? mbar_wait_cl(bar, parity, abort_flag) : mbar_wait(bar, parity, abort_flag)) ? 1 : 0;
+  ok = __shfl_sync(0xffffffffu, ok, 0);
+  if (ok) (void)(CL ? mbar_wait_cl(bar, parity, abort_flag) : mbar_wait(bar, parity, abort_flag));
+  return ok != 0;
+}
+
+// Arrival on a barrier the MMA issuer waits on: this CTA's own, or in a CTA
+// pair the leader's (even CTA) through its cluster address, with release at
+// cluster scope.
+template <bool PAIR>
+__device__ __forceinline__ void arrive_to_leader(uint64_t* bar) {
+  if constexpr (PAIR)
+    tc::mbar_arrive_cluster(tc::mapa_shared(bar, 0));
+  else
+    mbar_arrive(bar);
+}
+
+// The softmax role of both tensor-core prefill kernels: warps 0-7 of a CTA,
+// 128 query rows (rows q0 .. q0 + 127 of sequence b, head h) against the
+// n_tiles KV tiles of 128 keys.  Stages Q (pre-scaled, hi / lo parts) in
+// shared memory, turns each S tile of its warpgroup into P in tensor memory,
+// and writes O / l to `out` in the epilogue.  C supplies the shared-memory
+// and tensor-memory offsets; PAIR: the CTA is one of a cta_group::2 pair
+// whose leader issues the MMAs.
+template <typename T, int D, typename C, bool PAIR>
+__device__ __forceinline__ void softmax_role(const Params& p, unsigned char* smem, uint32_t tmem,
+                                             Bars bars, int32_t* abort_s, int warp, int lane,
+                                             int64_t b, int64_t h, int64_t q0, int64_t ctx,
+                                             int n_tiles) {
+  uint64_t* s_full = bars.s_full;
+  uint64_t* p_full = bars.p_full;
+  uint64_t* o_ready = bars.o_ready;
+  uint64_t* q_ready = bars.q_ready;
+  uint64_t* pair_bar = bars.pair_bar;
+  // Warp w serves query rows 32 * (w % 4) .. +31 (its TMEM lane quadrant)
+  // of the tiles of warpgroup w / 4.
+  const int quad = warp & 3;
+  const int r = quad * 32 + lane;  // query row in the tile = TMEM lane
+  const int64_t qrow = q0 + r;
+  const bool row_valid = qrow < p.Sq;
+  const int64_t q_abs = ctx - p.Sq + qrow;  // absolute position of this query
+  // Q tile -> shared memory, pre-scaled, hi (+ lo) parts, swizzled: warp w
+  // converts rows 16w .. 16w+15.
+  {
+    unsigned char* qh = smem + C::OFF_QH;
+    unsigned char* ql = smem + C::OFF_QL;
+    constexpr int EPT = D / 32;  // elements per lane per row
+    constexpr int RPW = BM / kSoftmaxWarps;  // rows per warp
+    // every row's global load is issued before the first shared store, so
+    // the warp waits on global memory once
+    float x[RPW][EPT];
+#pragma unroll
+    for (int i = 0; i < RPW; ++i) {
+      const int64_t qr = q0 + warp * RPW + i;
+      const float* src = p.q + ((b * p.Sq + qr) * p.H + h) * D + lane * EPT;
+      if constexpr (EPT == 4) {
+        const float4 v = qr < p.Sq ? __ldg(reinterpret_cast<const float4*>(src)) : make_float4(0.f, 0.f, 0.f, 0.f);
+        x[i][0] = v.x, x[i][1] = v.y, x[i][2] = v.z, x[i][3] = v.w;
+      } else {
+#pragma unroll
+        for (int e = 0; e < EPT; e += 2) {
+          const float2 v = qr < p.Sq ? __ldg(reinterpret_cast<const float2*>(src + e)) : make_float2(0.f, 0.f);
+          x[i][e] = v.x, x[i][e + 1] = v.y;
+        }
+      }
+    }
+#pragma unroll
+    for (int i = 0; i < RPW; ++i) {
+      const int rr = warp * RPW + i;
+#pragma unroll
+      for (int e = 0; e < EPT; e += 2) {
+        const uint32_t off = sw128_offset(rr, lane * EPT + e, BM);
+        uint32_t hi, lo;
+        split_pair(x[i][e] * p.qscale, x[i][e + 1] * p.qscale, hi, lo, (T*)nullptr);
+        *reinterpret_cast<uint32_t*>(qh + off) = hi;
+        if constexpr (C::SPLIT) *reinterpret_cast<uint32_t*>(ql + off) = lo;
+      }
+    }
+    tc::fence_proxy_async_smem();
+    arrive_to_leader<PAIR>(q_ready);
+  }
+
+  // Warpgroup g = warp / 4 takes the KV tiles j with j % 2 == g (S buffer
+  // g) and keeps, per query row, its own running reference max, sum and O
+  // accumulator (TMEM columns COL_O + g * D); the two partial states are
+  // merged with the log-sum-exp rule once, after the last tile.  Two tiles'
+  // softmax are in flight at a time and no cross-warp reduction sits on the
+  // per-tile path.
+  const int grp = warp >> 2;
+  const uint32_t lane_base = tmem + ((uint32_t)(quad * 32) << 16);
+  const uint32_t ocol = C::COL_O + grp * D;
+  float m_ref = -INFINITY, l = 0.f;
+  bool ok = true;
+  int last_j = -1;
+  for (int j = grp; j < n_tiles && ok; j += 2) {
+    if (!warp_wait_t<PAIR>(&s_full[grp], (j >> 1) & 1, abort_s)) { ok = false; break; }
+    tc::fence_after_sync();
+    const uint32_t scol = grp ? C::COL_S1 : C::COL_S0;
+    // causal rule + context bound (kernels/paged_attn_prefill.cu:62-65):
+    // keys k0 + c of this tile are visible when c < lim
+    const int64_t k0 = (int64_t)j * BN;
+    const int64_t vis = row_valid ? min(q_abs + 1, ctx) - k0 : 0;
+    const int lim = vis <= 0 ? 0 : (vis >= BN ? BN : (int)vis);
+    // pass 1: row max over the visible keys (S streamed from TMEM, 32
+    // columns at a time); tiles with every key visible to all of the warp's
+    // rows skip the per-key mask
+    const bool full = __all_sync(0xffffffffu, lim == BN);
+    float mt = -INFINITY;
+    if (full) {
+      float m4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+#pragma unroll
+      for (int c4 = 0; c4 < BN / 32; ++c4) {
+        uint32_t u[32];
+        tc::tmem_ld32(lane_base + scol + 32 * c4, u);
+        tc::tmem_wait_ld();
+#pragma unroll
+        for (int i = 0; i < 32; ++i) m4[i & 3] = fmaxf(m4[i & 3], __uint_as_float(u[i]));
+      }
+      mt = fmaxf(fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3]));
+    } else {
+#pragma unroll
+      for (int c4 = 0; c4 < BN / 32; ++c4) {
+        uint32_t u[32];
+        tc::tmem_ld32(lane_base + scol + 32 * c4, u);
+        tc::tmem_wait_ld();
+#pragma unroll
+        for (int i = 0; i < 32; ++i)
+          if (32 * c4 + i < lim) mt = fmaxf(mt, __uint_as_float(u[i]));
+      }
+    }
+    // The reference max of a row moves only when the row's max grows by more
+    // than 2^8 (then this group's O and l are rescaled); the O rescale is
+    // done by the whole warp (tcgen05.ld/st are warp-collective), factor 1
+    // for rows that keep their reference.
+    const bool need = mt > m_ref + 8.f;
+    const float factor = need ? fast_exp2(m_ref - mt) : 1.f;  // 0 on a row's first visible tile
+    if (__any_sync(0xffffffffu, need) && j >= 2) {
+      // the group's previous P V (tile j - 2) must have finished
+      if (!warp_wait_t<PAIR>(&o_ready[grp], ((j >> 1) - 1) & 1, abort_s)) { ok = false; break; }
+      tc::fence_after_sync();
+#pragma unroll
+      for (int c4 = 0; c4 < D / 32; ++c4) {
+        uint32_t u[32];
+        tc::tmem_ld32(lane_base + ocol + 32 * c4, u);
+        tc::tmem_wait_ld();
+#pragma unroll
+        for (int i = 0; i < 32; ++i) u[i] = __float_as_uint(__uint_as_float(u[i]) * factor);
+        tc::tmem_st32(lane_base + ocol + 32 * c4, u);
+      }
+      tc::tmem_wait_st();
+    }
+    if (need) {
+      l *= factor;
+      m_ref = mt;
+    }
+    // (V rows of keys past the context arrive zeroed from the TMA warp.)
+    // pass 2: P = exp2(s - m_ref) into the S columns, 32 keys at a time
+    // (S re-read from TMEM).  Keys 32c .. 32c + 31 go to columns
+    // [32c, 32c + 16) as 16-bit pairs (keys 2i, 2i+1 in column 32c + i),
+    // their lo parts to [32c + 16, 32c + 32): every store lands on columns
+    // this pass has already read.  Masked keys get s = -inf, so P = 0.
+    // (a row with no visible key so far has m_ref = -inf and only masked keys here)
+    const float mneg = m_ref == -INFINITY ? 0.f : -m_ref;
+    const float2 negm = make_float2(mneg, mneg);
+    float2 ls = make_float2(0.f, 0.f);
+#pragma unroll
+    for (int c = 0; c < BN / 32; ++c) {
+      uint32_t u[32];
+      tc::tmem_ld32(lane_base + scol + 32 * c, u);
+      tc::tmem_wait_ld();
+      if (!full) {
+#pragma unroll
+        for (int i = 0; i < 32; ++i)
+          if (32 * c + i >= lim) u[i] = __float_as_uint(-INFINITY);
+      }
+      uint32_t uh[16], ul[16];
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {
+        const float2 x = add2(make_float2(__uint_as_float(u[2 * i]), __uint_as_float(u[2 * i + 1])), negm);
+        const float2 e = make_float2(fast_exp2(x.x), fast_exp2(x.y));
+        ls = add2(ls, e);
+        p_pair(e.x, e.y, uh[i], ul[i], (T*)nullptr);
+      }
+      tc::tmem_st16(lane_base + scol + 32 * c, uh);
+      if constexpr (C::SPLIT) tc::tmem_st16(lane_base + scol + 32 * c + 16, ul);
+    }
+    const float lsum = ls.x + ls.y;
+    l += lsum;
+    tc::tmem_wait_st();
+    tc::fence_before_sync();
+    arrive_to_leader<PAIR>(&p_full[grp]);
+    last_j = j;
+  }
+
+  // epilogue: merge the two groups' (m, l, O) per row, O / l -> out.  Each
+  // warp of a pair writes half of the columns.  (m, l) cross through TMEM
+  // columns of this group's (now idle) S buffer.
+  const uint32_t xcol = grp ? C::COL_S1 : C::COL_S0;
+  const uint32_t xcol_other = grp ? C::COL_S0 : C::COL_S1;
+  float mo = -INFINITY, lo_ = 0.f;
+  bool have_mine = false, have_other = false;
+  if (ok) {
+    // all of this row's P V products must be complete: wait both groups' last
+    const int lj[2] = {n_tiles >= 1 ? ((n_tiles - 1) & ~1) : -1,
+                       n_tiles >= 2 ? (((n_tiles - 2) & ~1) | 1) : -1};
+    for (int g = 0; g < 2 && ok; ++g)
+      if (lj[g] >= 0 && !warp_wait_t<PAIR>(&o_ready[g], (lj[g] >> 1) & 1, abort_s)) ok = false;
+    have_mine = lj[grp] >= 0;
+    have_other = lj[grp ^ 1] >= 0;
+    (void)last_j;
+  }
+  if (ok) {
+    tc::fence_after_sync();
+    uint32_t x[32];
+    x[0] = __float_as_uint(m_ref);
+    x[1] = __float_as_uint(l);
+#pragma unroll
+    for (int i = 2; i < 32; ++i) x[i] = 0;
+    tc::tmem_st32(lane_base + xcol, x);
+    tc::tmem_wait_st();
+    tc::fence_before_sync();
+    mbar_arrive(&pair_bar[quad]);
+    if (warp_wait_t<false>(&pair_bar[quad], 0, abort_s)) {
+      tc::fence_after_sync();
+      uint32_t y[32];
+      tc::tmem_ld32(lane_base + xcol_other, y);
+      tc::tmem_wait_ld();
+      mo = __uint_as_float(y[0]);
+      lo_ = __uint_as_float(y[1]);
+    } else {
+      ok = false;
+    }
+  }
+  constexpr int HD = D / 2;
+  float o[HD];
+#pragma unroll
+  for (int i = 0; i < HD; ++i) o[i] = 0.f;
+  if (ok) {
+    // this warp's output columns [grp * HD, grp * HD + HD) from both O buffers
+    const float mA = grp ? mo : m_ref, lA = grp ? lo_ : l;
+    const float mB = grp ? m_ref : mo, lB = grp ? l : lo_;
+    const bool hasA = grp ? have_other : have_mine, hasB = grp ? have_mine : have_other;
+    const float mm = fmaxf(hasA ? mA : -INFINITY, hasB ? mB : -INFINITY);
+    const float wA = (hasA && lA > 0.f) ? fast_exp2(mA - mm) : 0.f;
+    const float wB = (hasB && lB > 0.f) ? fast_exp2(mB - mm) : 0.f;
+    const float L = lA * wA + lB * wB;
+    const float inv = L > 0.f ? 1.f / L : 0.f;
+#pragma unroll
+    for (int c4 = 0; c4 < HD / 32; ++c4) {
+      uint32_t ua[32], ub[32];
+      tc::tmem_ld32(lane_base + C::COL_O + grp * HD + 32 * c4, ua);
+      tc::tmem_ld32(lane_base + C::COL_O + D + grp * HD + 32 * c4, ub);
+      tc::tmem_wait_ld();
+#pragma unroll
+      for (int i = 0; i < 32; ++i) {
+        const float a = wA > 0.f ? __uint_as_float(ua[i]) * wA : 0.f;
+        const float bb = wB > 0.f ? __uint_as_float(ub[i]) * wB : 0.f;
+        o[32 * c4 + i] = (a + bb) * inv;
+      }
+    }
+  }
+  if (row_valid) {
+    float* dst = p.out + ((b * p.Sq + qrow) * p.H + h) * D + grp * HD;
+#pragma unroll
+    for (int i = 0; i < HD; i += 4)
+      *reinterpret_cast<float4*>(dst + i) = make_float4(o[i], o[i + 1], o[i + 2], o[i + 3]);
+  }
+  if (!ok && lane == 0) report(p.dev_status, PA_DEVERR_TIMEOUT);
+}
+
+// Host: the CTA-pair kernel for head_dim 128 (prefill_pair.cu).
+int launch_pair(const Params& p, int dtype, cudaStream_t s);
+
+// Host: tensor map of one pool tensor as [D, HKV, NB * BS] with a 64 x 1 x 16
+// box and 128-byte swizzle (prefill_tc.cu).
+int make_map(CUtensorMap* m, const void* base, int dtype, int64_t D, int64_t HKV, int64_t rows);
+
+}  // namespace prefill
+}  // namespace pa

@@ -68,32 +68,81 @@ template <> __device__ __forceinline__ __nv_fp8_e4m3 from_f32<__nv_fp8_e4m3>(flo
   return r;
 }
 
-// VEC: 8 elements per thread with vector loads/stores (needs D % 8 == 0 and
-// 16-byte aligned rows); otherwise one element per thread.
+// One pool element group: E elements of source row (l, kv, h, t) from `src`
+// converted into `dst` (VEC: 8 elements with 16-byte accesses, else 1).
 template <typename S, typename P, bool VEC>
-__global__ void __launch_bounds__(256) write_kv_kernel(const __grid_constant__ Params p) {
-  constexpr int E = VEC ? 8 : 1;
-  const int64_t per_row = p.D / E;
-  const int64_t rows = p.L * 2 * p.T * p.HKV;
-  const int64_t total = rows * per_row;
-  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
-  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += stride) {
-    const int64_t chunk = i % per_row;
-    int64_t row = i / per_row;
-    const int64_t h = row % p.HKV;
-    row /= p.HKV;
-    const int64_t t = row % p.T;
-    row /= p.T;
-    const int kv = (int)(row % 2);
-    const int64_t l = row / 2;
+__device__ __forceinline__ void convert_chunk(const S* src, P* dst, float qs) {
+  if constexpr (VEC) {
+    float f[8];
+    if constexpr (sizeof(S) == 4) {
+      const float4 a = __ldcs(reinterpret_cast<const float4*>(src));
+      const float4 b = __ldcs(reinterpret_cast<const float4*>(src) + 1);
+      f[0] = a.x; f[1] = a.y; f[2] = a.z; f[3] = a.w;
+      f[4] = b.x; f[5] = b.y; f[6] = b.z; f[7] = b.w;
+    } else {
+      const uint4 u = __ldcs(reinterpret_cast<const uint4*>(src));
+      const S* s8 = reinterpret_cast<const S*>(&u);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) f[e] = to_f32<S>(s8[e]);
+    }
+    if constexpr (sizeof(P) == 1) {
+      uint2 u;
+      P* d8 = reinterpret_cast<P*>(&u);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) d8[e] = from_f32<P>(__fdiv_rn(f[e], qs));
+      *reinterpret_cast<uint2*>(dst) = u;
+    } else if constexpr (sizeof(P) == 2) {
+      uint4 u;
+      P* d8 = reinterpret_cast<P*>(&u);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) d8[e] = from_f32<P>(f[e]);
+      *reinterpret_cast<uint4*>(dst) = u;
+    } else if constexpr (sizeof(P) == 4) {
+      reinterpret_cast<float4*>(dst)[0] = make_float4(f[0], f[1], f[2], f[3]);
+      reinterpret_cast<float4*>(dst)[1] = make_float4(f[4], f[5], f[6], f[7]);
+    } else {
+#pragma unroll
+      for (int e = 0; e < 8; e += 2)
+        reinterpret_cast<double2*>(dst)[e / 2] = make_double2((double)f[e], (double)f[e + 1]);
+    }
+  } else {
+    if constexpr (sizeof(P) == 1)
+      *dst = from_f32<P>(__fdiv_rn(to_f32<S>(*src), qs));
+    else
+      *dst = from_f32<P>(to_f32<S>(*src));
+  }
+}
 
+// Work unit = one token row (layer l, K or V, source token t): all HKV heads
+// x D elements of that token, which land contiguously in one page row of the
+// pool.  A CTA takes `rpi` rows per iteration (several when a row has fewer
+// element groups than the CTA has threads); the row's position, page and
+// block id are resolved once per row, and the head / group split of an
+// element group is a shift when D / E is a power of two.
+template <typename S, typename P, bool VEC>
+__global__ void __launch_bounds__(256) write_kv_kernel(const __grid_constant__ Params p,
+                                                       int32_t per_tok, int32_t per_head_shift,
+                                                       int32_t rpi) {
+  constexpr int E = VEC ? 8 : 1;
+  const int32_t per_head = (int32_t)(p.D / E);
+  const int64_t n_rows = p.L * 2 * p.T;
+  const int sub = threadIdx.x / per_tok;  // row within this CTA's iteration
+  const int32_t c0 = threadIdx.x - sub * per_tok;
+  const int32_t cstep = rpi > 1 ? per_tok : (int32_t)blockDim.x;
+  if (sub >= rpi) return;
+  for (int64_t row = (int64_t)blockIdx.x * rpi + sub; row < n_rows;
+       row += (int64_t)gridDim.x * rpi) {
+    const int64_t t = row % p.T;
+    const int64_t lk = row / p.T;
+    const int kv = (int)(lk & 1);
+    const int64_t l = lk >> 1;
     int64_t pos, page, blk;
     if (p.positions) {
       pos = p.positions[t];
       if (pos < 0) continue;
       page = pos / p.BS;
       if (page >= p.n_ids) {  // past the sequence's block table
-        if (chunk == 0) report(p.dev_status, PA_DEVERR_CONTEXT);
+        if (c0 == 0) report(p.dev_status, PA_DEVERR_CONTEXT);
         continue;
       }
       blk = p.block_ids[t * p.n_ids + page];
@@ -101,78 +150,55 @@ __global__ void __launch_bounds__(256) write_kv_kernel(const __grid_constant__ P
       pos = p.start + t;
       page = pos / p.BS;
       if (page >= p.n_ids) {
-        if (chunk == 0) report(p.dev_status, PA_DEVERR_BLOCK_ID);
+        if (c0 == 0) report(p.dev_status, PA_DEVERR_BLOCK_ID);
         continue;
       }
       blk = p.block_ids[page];
     }
     if (blk < 0 || blk >= p.NB) {
-      if (chunk == 0) report(p.dev_status, PA_DEVERR_BLOCK_ID);
+      if (c0 == 0) report(p.dev_status, PA_DEVERR_BLOCK_ID);
       continue;
     }
     const S* src = reinterpret_cast<const S*>(kv ? p.v_src : p.k_src) + l * p.src_layer_stride +
-                   h * p.src_head_stride + t * p.src_token_stride + chunk * E;
+                   t * p.src_token_stride;
     P* dst = reinterpret_cast<P*>(kv ? p.v_layers[l] : p.k_layers[l]) +
-             ((blk * p.BS + (pos - page * p.BS)) * p.HKV + h) * p.D + chunk * E;
-    float qs = 1.f;  // FP8: stored value = x / scale
-    if constexpr (sizeof(P) == 1) {
-      const float* sc = kv ? p.v_scales : p.k_scales;
-      if (sc) qs = sc[l * p.HKV + h];
-    }
-    if constexpr (VEC) {
-      float f[8];
-      if constexpr (sizeof(S) == 4) {
-        const float4 a = reinterpret_cast<const float4*>(src)[0];
-        const float4 b = reinterpret_cast<const float4*>(src)[1];
-        f[0] = a.x; f[1] = a.y; f[2] = a.z; f[3] = a.w;
-        f[4] = b.x; f[5] = b.y; f[6] = b.z; f[7] = b.w;
-      } else {
-        const uint4 u = *reinterpret_cast<const uint4*>(src);
-        const S* s8 = reinterpret_cast<const S*>(&u);
-#pragma unroll
-        for (int e = 0; e < 8; ++e) f[e] = to_f32<S>(s8[e]);
-      }
+             (blk * p.BS + (pos - page * p.BS)) * p.HKV * p.D;
+    const float* sc = kv ? p.v_scales : p.k_scales;
+    for (int32_t c = c0; c < per_tok; c += cstep) {
+      const int32_t h = per_head_shift >= 0 ? (c >> per_head_shift) : c / per_head;
+      const int32_t ch = c - h * per_head;
+      float qs = 1.f;  // FP8: stored value = x / scale
       if constexpr (sizeof(P) == 1) {
-        uint2 u;
-        P* d8 = reinterpret_cast<P*>(&u);
-#pragma unroll
-        for (int e = 0; e < 8; ++e) d8[e] = from_f32<P>(__fdiv_rn(f[e], qs));
-        *reinterpret_cast<uint2*>(dst) = u;
-      } else if constexpr (sizeof(P) == 2) {
-        uint4 u;
-        P* d8 = reinterpret_cast<P*>(&u);
-#pragma unroll
-        for (int e = 0; e < 8; ++e) d8[e] = from_f32<P>(f[e]);
-        *reinterpret_cast<uint4*>(dst) = u;
-      } else if constexpr (sizeof(P) == 4) {
-        reinterpret_cast<float4*>(dst)[0] = make_float4(f[0], f[1], f[2], f[3]);
-        reinterpret_cast<float4*>(dst)[1] = make_float4(f[4], f[5], f[6], f[7]);
-      } else {
-#pragma unroll
-        for (int e = 0; e < 8; e += 2)
-          reinterpret_cast<double2*>(dst)[e / 2] = make_double2((double)f[e], (double)f[e + 1]);
+        if (sc) qs = sc[l * p.HKV + h];
       }
-    } else {
-      if constexpr (sizeof(P) == 1)
-        *dst = from_f32<P>(__fdiv_rn(to_f32<S>(*src), qs));
-      else
-        *dst = from_f32<P>(to_f32<S>(*src));
+      convert_chunk<S, P, VEC>(src + h * p.src_head_stride + (int64_t)ch * E,
+                               dst + (int64_t)c * E, qs);
     }
   }
 }
 
 template <typename S, typename P>
 static int launch_typed(const Params& p, bool vec, cudaStream_t s) {
-  const int64_t per_row = vec ? p.D / 8 : p.D;
-  const int64_t total = p.L * 2 * p.T * p.HKV * per_row;
-  if (total == 0) return PA_OK;
+  const int64_t per_head = vec ? p.D / 8 : p.D;
+  const int64_t per_tok = p.HKV * per_head;
+  const int64_t n_rows = p.L * 2 * p.T;
+  if (n_rows == 0 || per_tok == 0) return PA_OK;
+  if (per_tok > (int64_t(1) << 30)) return PA_ERR_TOO_LARGE;
   int sms = 148;
   if (device_sm_count(&sms) != PA_OK) return PA_ERR_NO_DEVICE;
-  const int64_t blocks = std::max<int64_t>(1, std::min<int64_t>((total + 255) / 256, (int64_t)sms * 16));
+  constexpr int kThreads = 256;
+  const int rpi = per_tok >= kThreads ? 1 : (int)(kThreads / per_tok);
+  int shift = -1;
+  if ((per_head & (per_head - 1)) == 0) {
+    shift = 0;
+    while ((int64_t(1) << shift) < per_head) ++shift;
+  }
+  const int64_t blocks =
+      std::max<int64_t>(1, std::min<int64_t>((n_rows + rpi - 1) / rpi, (int64_t)sms * 16));
   if (vec)
-    write_kv_kernel<S, P, true><<<(unsigned)blocks, 256, 0, s>>>(p);
+    write_kv_kernel<S, P, true><<<(unsigned)blocks, kThreads, 0, s>>>(p, (int32_t)per_tok, shift, rpi);
   else
-    write_kv_kernel<S, P, false><<<(unsigned)blocks, 256, 0, s>>>(p);
+    write_kv_kernel<S, P, false><<<(unsigned)blocks, kThreads, 0, s>>>(p, (int32_t)per_tok, shift, rpi);
   return cuda_status(cudaGetLastError());
 }
 

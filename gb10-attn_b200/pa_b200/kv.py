@@ -232,6 +232,24 @@ class TorchBlockAllocator:
                       self.v_scales if self.fp8 else empty)
 
     # -- writer ----------------------------------------------------------------
+    _IDS_CACHE_MAX = 4096
+
+    def _device_ids(self, block_ids) -> torch.Tensor:
+        """Device int32 copy of a block-id list, kept by content: a sequence
+        written chunk by chunk (or re-written) reuses its copy, so the writer
+        does not upload its block ids from pageable memory on every call (a
+        synchronous copy that would stall the stream)."""
+        arr = np.ascontiguousarray(np.asarray(block_ids, dtype=np.int32).reshape(-1))
+        key = arr.tobytes()
+        cache = self.__dict__.setdefault("_ids_cache", {})
+        ids = cache.pop(key, None)
+        if ids is None:
+            ids = torch.from_numpy(arr.copy()).to(self.device)
+            if len(cache) >= self._IDS_CACHE_MAX:
+                cache.pop(next(iter(cache)))
+        cache[key] = ids  # most recently used last
+        return ids
+
     def write_kv(self, block_ids, start: int, k, v) -> None:
         """Write K/V of one sequence for every layer.
 
@@ -246,12 +264,10 @@ class TorchBlockAllocator:
                 t = t.pin_memory().to(self.device, non_blocking=True)
             return t
 
-        # a few hundred bytes: one plain copy (pinning a fresh host buffer per
-        # call would cost far more than the copy)
         if isinstance(block_ids, torch.Tensor):
             ids = block_ids.to(device=self.device, dtype=torch.int32)
         else:
-            ids = torch.as_tensor(np.asarray(block_ids, dtype=np.int32)).to(self.device)
+            ids = self._device_ids(block_ids)
         n_layer = self.model_cfg.n_layer
         ks = [self.pool[layer, 0] for layer in range(n_layer)]
         vs = [self.pool[layer, 1] for layer in range(n_layer)]
