@@ -44,7 +44,6 @@ template <typename T>
 struct PairCfg {
   static constexpr int D = 128;
   static constexpr bool SPLIT = Fmt<T>::split;
-  static constexpr int NH = 2;                          // 64-column halves of a row
   static constexpr uint32_t Q_BYTES = BM * D * 2;       // one Q part: 2 halves x 128 rows x 128 B
   static constexpr int KROWS = BN / 2;                  // keys of a K tile per CTA
   static constexpr uint32_t K_BYTES = KROWS * D * 2;    // 2 halves x 64 rows x 128 B
@@ -61,8 +60,11 @@ struct PairCfg {
   // pair barriers; then the TMEM address and the abort flag
   static constexpr uint32_t N_BARS = 2 * NK + 2 * NV + 2 * 3 + 1 + 4;
   static constexpr uint32_t OFF_BT = OFF_BAR + ((N_BARS * 8 + 8 + 15) / 16) * 16;
-  static constexpr uint32_t SMEM = OFF_BT + kBtChunk * 4 + 1024;  // + alignment slack
+  // two block-id chunks: one per loading warp (K, V)
+  static constexpr uint32_t OFF_XCH = OFF_BT + 2 * kBtChunk * 4;    // [2][2][128] fp32
+  static constexpr uint32_t SMEM = OFF_XCH + 2048 + 1024;            // + alignment slack
   static_assert(SMEM <= 227 * 1024, "shared memory budget");
+  // TMEM columns: S buffers at 0 and 128 (tiles j % 2), O at 256
   static constexpr uint32_t COL_S0 = 0, COL_S1 = 128, COL_O = 256;
 };
 
@@ -83,11 +85,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
   uint64_t* k_empty = k_full + NK;    // [NK] S = Q K^T done with the stage (both CTAs)
   uint64_t* v_full = k_empty + NK;    // [NV] leader: both V halves landed / written
   uint64_t* v_empty = v_full + NV;    // [NV] P V done with the stage (both CTAs)
-  uint64_t* s_full = v_empty + NV;    // [2] S tile in tensor memory (both CTAs)
-  uint64_t* p_full = s_full + 2;      // [2] leader: P of both CTAs written
-  uint64_t* o_ready = p_full + 2;     // [2] P V of a tile of group j % 2 done (both CTAs)
+  uint64_t* s_full = v_empty + NV;    // [2] S of tile j in tensor memory (both CTAs)
+  uint64_t* p_full = s_full + 2;      // [2] leader: P of tile j written in both CTAs
+  uint64_t* o_ready = p_full + 2;     // [2] P V of tile j done (both CTAs)
   uint64_t* q_ready = o_ready + 2;    // leader: Q of both CTAs staged
-  uint64_t* pair_bar = q_ready + 1;   // [4] (m, l) exchange inside the CTA
+  uint64_t* pair_bar = q_ready + 1;   // [4] row max / sum exchange inside the CTA
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(pair_bar + 4);
   int32_t* abort_s = reinterpret_cast<int32_t*>(tmem_slot + 1);
 
@@ -116,7 +118,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     }
     for (int s = 0; s < 2; ++s) {
       mbar_init(&s_full[s], 1);
-      mbar_init(&p_full[s], 2 * 4 * 32);  // one warpgroup of each CTA per tile
+      mbar_init(&p_full[s], 2 * kSoftmaxWarps * 32);  // both warpgroups of both CTAs
       mbar_init(&o_ready[s], 1);
     }
     mbar_init(q_ready, 2 * kSoftmaxWarps * 32);
@@ -144,11 +146,18 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
   const int64_t q_last = min(pq0 + 2 * BM, p.Sq) - 1;
   const int64_t key_end = min(ctx, ctx - p.Sq + q_last + 1);
   const int n_tiles = key_end > 0 ? (int)((key_end + BN - 1) / BN) : 0;
+  // The pairs of one head run side by side and share its K/V in L2; each
+  // starts its walk over the KV tiles at a different tile, so they do not all
+  // request the same lines at the same moment.
+  const int rot = n_tiles > 0 ? (int)((c * 7) % n_tiles) : 0;
+  auto phys = [&](int j) { return j + rot < n_tiles ? j + rot : j + rot - n_tiles; };
 
   if (warp < kSoftmaxWarps) {
     asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kSoftmaxRegs));
-    softmax_role<T, D, C, true>(p, smem, tmem, Bars{s_full, p_full, o_ready, q_ready, pair_bar},
-                                abort_s, warp, lane, b, h, q0, ctx, n_tiles);
+    softmax_role<T, D, C, true>(p, smem, tmem,
+                                Bars{s_full, p_full, o_ready, q_ready, pair_bar,
+                                     reinterpret_cast<float*>(smem + C::OFF_XCH)},
+                                abort_s, warp, lane, b, h, q0, ctx, n_tiles, rot);
   } else {
    asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kOtherRegs));
    if (warp == kMmaWarp) {
@@ -194,10 +203,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
 #pragma unroll
           for (int kk = 0; kk < BN / 16; ++kk) {
             // keys 16kk .. 16kk + 15: 8 columns of packed pairs
-            tc::mma_ts_pair(tmem + C::COL_O + (j & 1) * D,
-                            pcol + (kk >> 1) * 32 + (kk & 1) * 8 + part * 16,
+            tc::mma_ts_pair(tmem + C::COL_O, pcol + (kk >> 1) * 32 + (kk & 1) * 8 + part * 16,
                             tc::smem_desc_sw128(vb + kk * 16 * 128, BN * 128, 1024), idesc_o,
-                            (j > 1 || part > 0 || kk > 0) ? 1u : 0u);
+                            (j > 0 || part > 0 || kk > 0) ? 1u : 0u);
           }
         }
         tc::mma_commit_pair(&v_empty[vs], kBoth);
@@ -205,13 +213,17 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       }
       if (!ok) report(p.dev_status, PA_DEVERR_TIMEOUT);
     }
-   } else if (warp == kTmaWarp) {
-    // ------------------------------------------------- TMA producer (both CTAs)
+   } else if (warp == kTmaWarp || warp == kTmaWarp + 1) {
+    // ------------------------------------- TMA producers (both CTAs): K and V
+    // Warp 9 loads K, warp 10 loads V, each issuing its own copies (one warp
+    // issuing both measured half the load rate the MMAs need).
     // K: lane l < 8 loads 16 keys (group l >> 1 of this CTA's 64) x half l & 1;
     // V: lane l < 8 loads 16 keys (group l of the tile's 128) x this CTA's
-    // half.  The block ids are staged in shared memory as in prefill_tc.cu.
+    // half.  The block ids are staged in shared memory as in prefill_tc.cu,
+    // one chunk per warp.
+    const bool is_v = warp != kTmaWarp;
     const int32_t* bt = p.block_tables + b * p.MB;
-    int32_t* bt_s = reinterpret_cast<int32_t*>(smem + C::OFF_BT);
+    int32_t* bt_s = reinterpret_cast<int32_t*>(smem + C::OFF_BT) + (is_v ? kBtChunk : 0);
     const int64_t n_pages = (ctx + p.BS - 1) / p.BS;
     int64_t chunk0 = -(int64_t)kBtChunk - 1;
     auto stage_pages = [&](int64_t pg_lo, int64_t pg_hi) {
@@ -230,7 +242,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     };
     // pool row of the 16-token group at offset `toff` in tile j (0 past the context)
     auto group_row = [&](int j, int toff) -> int32_t {
-      const int64_t t0 = (int64_t)j * BN;
+      const int64_t t0 = (int64_t)phys(j) * BN;
       stage_pages(t0 / p.BS, (t0 + BN - 1) / p.BS);
       const int64_t t = t0 + toff;
       if (lane >= 8 || t >= ctx) return 0;
@@ -264,7 +276,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       const int32_t row = group_row(j, lane * 16);
       if (!warp_wait_t<true>(&v_empty[st], ((j / NV) & 1) ^ 1, abort_s)) return false;
       unsigned char* dst = smem + C::OFF_V + st * C::V_BYTES + lane * C::GROUP_BYTES;
-      const int64_t valid = ctx - ((int64_t)j * BN + lane * 16);
+      const int64_t valid = ctx - ((int64_t)phys(j) * BN + lane * 16);
       const bool manual = lane < 8 && valid < 16;
       if (manual) {
         v_group_sanitised(dst, p.v_pool, row, valid, p.HKV, kv_h, (int)rank, D);
@@ -284,14 +296,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                              tc::mapa_shared(&v_full[st], 0));
       return true;
     };
-    // K runs NK - NV tiles ahead of V
-    constexpr int AHEAD = NK - NV;
     bool ok = true;
-    for (int i = 0; i < AHEAD && i < n_tiles && ok; ++i) ok = load_k(i);
-    for (int j = 0; j < n_tiles && ok; ++j) {
-      if (j + AHEAD < n_tiles) ok = load_k(j + AHEAD);
-      if (ok) ok = load_v(j);
-    }
+    for (int j = 0; j < n_tiles && ok; ++j) ok = is_v ? load_v(j) : load_k(j);
     if (!ok && lane == 0) report(p.dev_status, PA_DEVERR_TIMEOUT);
    }
   }

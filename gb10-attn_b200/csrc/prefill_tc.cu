@@ -60,9 +60,9 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const __grid_co
   uint64_t* k_empty = k_full + NK;       // [NK] S = Q K^T done with it
   uint64_t* v_full = k_empty + NK;       // [NV] V tile landed
   uint64_t* v_empty = v_full + NV;       // [NV] P V done with it
-  uint64_t* s_full = v_empty + NV;       // [2] S tile in TMEM
-  uint64_t* p_full = s_full + 2;         // [2] P written to TMEM (softmax warps)
-  uint64_t* o_ready = p_full + 2;        // [2] P V of a tile of group j % 2 done
+  uint64_t* s_full = v_empty + NV;       // [2] S of tile j in TMEM (slot j % 2)
+  uint64_t* p_full = s_full + 2;         // [2] P of tile j written (both softmax warpgroups)
+  uint64_t* o_ready = p_full + 2;        // [2] P V of tile j done
   uint64_t* q_ready = o_ready + 2;       // Q in shared memory (softmax warps)
   uint64_t* pair_bar = q_ready + 1;     // [4] max / sum exchange of a warp pair (64 threads)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(pair_bar + 4);
@@ -90,7 +90,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const __grid_co
     }
     for (int s = 0; s < 2; ++s) {
       mbar_init(&s_full[s], 1);
-      mbar_init(&p_full[s], 4 * 32);  // one warpgroup per tile
+      mbar_init(&p_full[s], kSoftmaxWarps * 32);  // both warpgroups per tile
       mbar_init(&o_ready[s], 1);
     }
     mbar_init(q_ready, kSoftmaxWarps * 32);
@@ -121,8 +121,10 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const __grid_co
   if (warp < kSoftmaxWarps) {
     // ------------------------------------------------------------------ softmax
     asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kSoftmaxRegs));
-    softmax_role<T, D, C, false>(p, smem, tmem, Bars{s_full, p_full, o_ready, q_ready, pair_bar},
-                                 abort_s, warp, lane, b, h, q0, ctx, n_tiles);
+    softmax_role<T, D, C, false>(p, smem, tmem,
+                                 Bars{s_full, p_full, o_ready, q_ready, pair_bar,
+                                      reinterpret_cast<float*>(smem + C::OFF_XCH)},
+                                 abort_s, warp, lane, b, h, q0, ctx, n_tiles, 0);
   } else {
    asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kOtherRegs));
    if (warp == kMmaWarp) {
@@ -168,9 +170,9 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const __grid_co
 #pragma unroll
           for (int kk = 0; kk < BN / 16; ++kk) {
             // keys 16kk .. 16kk + 15: 8 columns of packed pairs
-            tc::mma_ts(tmem + C::COL_O + (j & 1) * D, pcol + (kk >> 1) * 32 + (kk & 1) * 8 + part * 16,
+            tc::mma_ts(tmem + C::COL_O, pcol + (kk >> 1) * 32 + (kk & 1) * 8 + part * 16,
                        tc::smem_desc_sw128(vb + kk * 16 * 128, BN * 128, 1024), idesc_o,
-                       (j > 1 || part > 0 || kk > 0) ? 1u : 0u);
+                       (j > 0 || part > 0 || kk > 0) ? 1u : 0u);
           }
         }
         tc::mma_commit(&v_empty[vs]);
@@ -372,10 +374,9 @@ int launch_tc(float* out, const float* q, const void* k, const void* v, int dtyp
   const int64_t grid = (int64_t)p.n_qtiles * B * H;
   if (grid <= 0) return PA_OK;
   if (grid > (int64_t(1) << 31) - 1) return PA_ERR_TOO_LARGE;
-  if (dtype == PA_DTYPE_BF16)
-    return D == 128 ? launch_typed<__nv_bfloat16, 128>(p, grid, s)
-                    : launch_typed<__nv_bfloat16, 64>(p, grid, s);
-  return D == 128 ? launch_typed<__half, 128>(p, grid, s) : launch_typed<__half, 64>(p, grid, s);
+  // head_dim 64 (head_dim 128 went to the pair kernel above)
+  return dtype == PA_DTYPE_BF16 ? launch_typed<__nv_bfloat16, 64>(p, grid, s)
+                                : launch_typed<__half, 64>(p, grid, s);
 }
 
 }  // namespace prefill

@@ -66,10 +66,10 @@ struct Cfg {
   // 4 pair barriers; then the TMEM address and the abort flag
   static constexpr uint32_t N_BARS = 2 * NK + 2 * NV + 2 * 3 + 1 + 4;
   static constexpr uint32_t OFF_BT = OFF_BAR + ((N_BARS * 8 + 8 + 15) / 16) * 16;
-  static constexpr uint32_t SMEM = OFF_BT + kBtChunk * 4 + 1024;  // + alignment slack
+  static constexpr uint32_t OFF_XCH = OFF_BT + kBtChunk * 4;      // [2][2][128] fp32
+  static constexpr uint32_t SMEM = OFF_XCH + 2048 + 1024;          // + alignment slack
   static_assert(SMEM <= 227 * 1024, "shared memory budget");
-  // TMEM columns: S buffers at 0 and 128 (tiles j % 2), O of the two
-  // softmax warpgroups at 256 and 256 + D
+  // TMEM columns: S buffers at 0 and 128 (tiles j % 2), O at 256
   static constexpr uint32_t COL_S0 = 0, COL_S1 = 128, COL_O = 256;
 };
 
@@ -170,11 +170,12 @@ __device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, int32_
 
 // Barriers the softmax warps use (this CTA's shared memory).
 struct Bars {
-  uint64_t* s_full;    // [2] S tile of group g in tensor memory (MMA commit)
-  uint64_t* p_full;    // [2] P of group g written (softmax arrivals; the leader's in a pair)
-  uint64_t* o_ready;   // [2] P V of group g done (MMA commit)
+  uint64_t* s_full;    // [2] S of tile j in tensor memory, slot j % 2 (MMA commit)
+  uint64_t* p_full;    // [2] P of tile j written by both groups (the leader's in a pair)
+  uint64_t* o_ready;   // [2] P V of tile j done, slot j % 2 (MMA commit)
   uint64_t* q_ready;   // Q staged (softmax arrivals; the leader's in a pair)
-  uint64_t* pair_bar;  // [4] (m, l) exchange of a warp pair
+  uint64_t* pair_bar;  // [4] row max / sum exchange of warps w and w + 4 (64 arrivals)
+  float* xch;          // [2][2][128] exchange slots (shared memory)
 };
 
 // Warp-uniform bounded wait; CL: acquire at cluster scope (barriers another
@@ -204,14 +205,16 @@ __device__ __forceinline__ void arrive_to_leader(uint64_t* bar) {
 // 128 query rows (rows q0 .. q0 + 127 of sequence b, head h) against the
 // n_tiles KV tiles of 128 keys.  Stages Q (pre-scaled, hi / lo parts) in
 // shared memory, turns each S tile of its warpgroup into P in tensor memory,
-// and writes O / l to `out` in the epilogue.  C supplies the shared-memory
+// and writes O / l to `out` in the epilogue.  Step j of the KV loop holds
+// KV tile (j + rot) % n_tiles (the online softmax does not depend on the
+// order).  C supplies the shared-memory
 // and tensor-memory offsets; PAIR: the CTA is one of a cta_group::2 pair
 // whose leader issues the MMAs.
 template <typename T, int D, typename C, bool PAIR>
 __device__ __forceinline__ void softmax_role(const Params& p, unsigned char* smem, uint32_t tmem,
                                              Bars bars, int32_t* abort_s, int warp, int lane,
                                              int64_t b, int64_t h, int64_t q0, int64_t ctx,
-                                             int n_tiles) {
+                                             int n_tiles, int rot) {
   uint64_t* s_full = bars.s_full;
   uint64_t* p_full = bars.p_full;
   uint64_t* o_ready = bars.o_ready;
@@ -249,6 +252,7 @@ __device__ __forceinline__ void softmax_role(const Params& p, unsigned char* sme
         }
       }
     }
+    bool qover = false;  // fp16 pools: a scaled q element outside the fp16 range
 #pragma unroll
     for (int i = 0; i < RPW; ++i) {
       const int rr = warp * RPW + i;
@@ -256,75 +260,90 @@ __device__ __forceinline__ void softmax_role(const Params& p, unsigned char* sme
       for (int e = 0; e < EPT; e += 2) {
         const uint32_t off = sw128_offset(rr, lane * EPT + e, BM);
         uint32_t hi, lo;
-        split_pair(x[i][e] * p.qscale, x[i][e + 1] * p.qscale, hi, lo, (T*)nullptr);
+        const float a = x[i][e] * p.qscale, bq = x[i][e + 1] * p.qscale;
+        if constexpr (!C::SPLIT) qover |= !(fabsf(a) < 65520.f && fabsf(bq) < 65520.f);
+        split_pair(a, bq, hi, lo, (T*)nullptr);
         *reinterpret_cast<uint32_t*>(qh + off) = hi;
         if constexpr (C::SPLIT) *reinterpret_cast<uint32_t*>(ql + off) = lo;
       }
     }
+    if (qover) report(p.dev_status, PA_DEVERR_RANGE);
     tc::fence_proxy_async_smem();
     arrive_to_leader<PAIR>(q_ready);
   }
 
-  // Warpgroup g = warp / 4 takes the KV tiles j with j % 2 == g (S buffer
-  // g) and keeps, per query row, its own running reference max, sum and O
-  // accumulator (TMEM columns COL_O + g * D); the two partial states are
-  // merged with the log-sum-exp rule once, after the last tile.  Two tiles'
-  // softmax are in flight at a time and no cross-warp reduction sits on the
-  // per-tile path.
+  // Both warpgroups work on every KV tile: group g = warp / 4 takes columns
+  // [64 g, 64 g + 64) of the S tile for the 128 query rows (warps w and w + 4
+  // hold the same rows, TMEM lane quadrant w % 4).  Per tile the two halves'
+  // row maxima meet through shared memory (xch, two slots, pair_bar[quad]
+  // bounded barrier), both groups then share one reference max per row, each
+  // writes P of its 64 keys and keeps its half of the row sum; O is one
+  // accumulator of which group g rescales columns [g D / 2, (g + 1) D / 2).
+  // The MMA issuer computes S of tile j + 1 while tile j's softmax runs.
   const int grp = warp >> 2;
   const uint32_t lane_base = tmem + ((uint32_t)(quad * 32) << 16);
-  const uint32_t ocol = C::COL_O + grp * D;
-  float m_ref = -INFINITY, l = 0.f;
+  constexpr int HD = D / 2;  // O columns per group
+  const uint32_t ocol = C::COL_O + grp * HD;
+  float* xch = bars.xch;     // [2 slots][2 groups][128 rows]
+  float m_ref = -INFINITY, l = 0.f;  // l: this group's half of the row sum
   bool ok = true;
-  int last_j = -1;
-  for (int j = grp; j < n_tiles && ok; j += 2) {
-    if (!warp_wait_t<PAIR>(&s_full[grp], (j >> 1) & 1, abort_s)) { ok = false; break; }
+  uint32_t xuses = 0;        // phases of pair_bar[quad] used so far
+  auto exchange = [&](float mine) -> float {  // the partner half's value of this row
+    float* xs = xch + (xuses & 1) * 256;
+    xs[grp * 128 + r] = mine;
+    mbar_arrive(&pair_bar[quad]);
+    if (!warp_wait_t<false>(&pair_bar[quad], xuses & 1, abort_s)) ok = false;
+    ++xuses;
+    return xs[(grp ^ 1) * 128 + r];
+  };
+  for (int j = 0; j < n_tiles && ok; ++j) {
+    const int sb = j & 1;
+    if (!warp_wait_t<PAIR>(&s_full[sb], (j >> 1) & 1, abort_s)) { ok = false; break; }
     tc::fence_after_sync();
-    const uint32_t scol = grp ? C::COL_S1 : C::COL_S0;
+    const uint32_t scol = (sb ? C::COL_S1 : C::COL_S0) + 64 * grp;
     // causal rule + context bound (kernels/paged_attn_prefill.cu:62-65):
-    // keys k0 + c of this tile are visible when c < lim
-    const int64_t k0 = (int64_t)j * BN;
-    const int64_t vis = row_valid ? min(q_abs + 1, ctx) - k0 : 0;
-    const int lim = vis <= 0 ? 0 : (vis >= BN ? BN : (int)vis);
-    // pass 1: row max over the visible keys (S streamed from TMEM, 32
-    // columns at a time); tiles with every key visible to all of the warp's
-    // rows skip the per-key mask
-    const bool full = __all_sync(0xffffffffu, lim == BN);
-    float mt = -INFINITY;
-    if (full) {
-      float m4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+    // keys k0 + c of this tile are visible when c < lim; this group's
+    // columns c = 64 grp + i are visible when i < mlim
+    const int jt = j + rot < n_tiles ? j + rot : j + rot - n_tiles;  // physical tile
+    const int64_t k0 = (int64_t)jt * BN;
+    const int64_t vis = row_valid ? min(q_abs + 1, ctx) - k0 - 64 * grp : 0;
+    const int mlim = vis <= 0 ? 0 : (vis >= 64 ? 64 : (int)vis);
+    const bool full = __all_sync(0xffffffffu, mlim == 64);
+    // This group's 64 scores of the row: two loads issued back to back, one
+    // wait; they stay in registers for the exponentials.  Masked keys become
+    // -inf (P = 0).
+    uint32_t sa[32], sb2[32];
+    tc::tmem_ld32(lane_base + scol, sa);
+    tc::tmem_ld32(lane_base + scol + 32, sb2);
+    tc::tmem_wait_ld();
+    if (!full) {
 #pragma unroll
-      for (int c4 = 0; c4 < BN / 32; ++c4) {
-        uint32_t u[32];
-        tc::tmem_ld32(lane_base + scol + 32 * c4, u);
-        tc::tmem_wait_ld();
-#pragma unroll
-        for (int i = 0; i < 32; ++i) m4[i & 3] = fmaxf(m4[i & 3], __uint_as_float(u[i]));
-      }
-      mt = fmaxf(fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3]));
-    } else {
-#pragma unroll
-      for (int c4 = 0; c4 < BN / 32; ++c4) {
-        uint32_t u[32];
-        tc::tmem_ld32(lane_base + scol + 32 * c4, u);
-        tc::tmem_wait_ld();
-#pragma unroll
-        for (int i = 0; i < 32; ++i)
-          if (32 * c4 + i < lim) mt = fmaxf(mt, __uint_as_float(u[i]));
+      for (int i = 0; i < 32; ++i) {
+        if (i >= mlim) sa[i] = __float_as_uint(-INFINITY);
+        if (32 + i >= mlim) sb2[i] = __float_as_uint(-INFINITY);
       }
     }
+    float m4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+#pragma unroll
+    for (int i = 0; i < 32; ++i) {
+      m4[i & 1] = fmaxf(m4[i & 1], __uint_as_float(sa[i]));
+      m4[2 + (i & 1)] = fmaxf(m4[2 + (i & 1)], __uint_as_float(sb2[i]));
+    }
+    const float pm = fmaxf(fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3]));
+    const float mt = fmaxf(pm, exchange(pm));
+    if (!ok) break;
     // The reference max of a row moves only when the row's max grows by more
-    // than 2^8 (then this group's O and l are rescaled); the O rescale is
-    // done by the whole warp (tcgen05.ld/st are warp-collective), factor 1
-    // for rows that keep their reference.
+    // than 2^8 (then O and l are rescaled); the O rescale is done by the
+    // whole warp (tcgen05.ld/st are warp-collective), factor 1 for rows that
+    // keep their reference.  Both groups reach the same decision per row.
     const bool need = mt > m_ref + 8.f;
     const float factor = need ? fast_exp2(m_ref - mt) : 1.f;  // 0 on a row's first visible tile
-    if (__any_sync(0xffffffffu, need) && j >= 2) {
-      // the group's previous P V (tile j - 2) must have finished
-      if (!warp_wait_t<PAIR>(&o_ready[grp], ((j >> 1) - 1) & 1, abort_s)) { ok = false; break; }
+    if (__any_sync(0xffffffffu, need) && j >= 1) {
+      // the previous tile's P V must have finished
+      if (!warp_wait_t<PAIR>(&o_ready[(j - 1) & 1], ((j - 1) >> 1) & 1, abort_s)) { ok = false; break; }
       tc::fence_after_sync();
 #pragma unroll
-      for (int c4 = 0; c4 < D / 32; ++c4) {
+      for (int c4 = 0; c4 < HD / 32; ++c4) {
         uint32_t u[32];
         tc::tmem_ld32(lane_base + ocol + 32 * c4, u);
         tc::tmem_wait_ld();
@@ -339,25 +358,14 @@ __device__ __forceinline__ void softmax_role(const Params& p, unsigned char* sme
       m_ref = mt;
     }
     // (V rows of keys past the context arrive zeroed from the TMA warp.)
-    // pass 2: P = exp2(s - m_ref) into the S columns, 32 keys at a time
-    // (S re-read from TMEM).  Keys 32c .. 32c + 31 go to columns
-    // [32c, 32c + 16) as 16-bit pairs (keys 2i, 2i+1 in column 32c + i),
-    // their lo parts to [32c + 16, 32c + 32): every store lands on columns
-    // this pass has already read.  Masked keys get s = -inf, so P = 0.
+    // P = exp2(s - m_ref) into this group's S columns: keys 32c .. 32c + 31
+    // go to columns [32c, 32c + 16) as 16-bit pairs (keys 2i, 2i+1 in column
+    // 32c + i), their lo parts to [32c + 16, 32c + 32).
     // (a row with no visible key so far has m_ref = -inf and only masked keys here)
     const float mneg = m_ref == -INFINITY ? 0.f : -m_ref;
     const float2 negm = make_float2(mneg, mneg);
     float2 ls = make_float2(0.f, 0.f);
-#pragma unroll
-    for (int c = 0; c < BN / 32; ++c) {
-      uint32_t u[32];
-      tc::tmem_ld32(lane_base + scol + 32 * c, u);
-      tc::tmem_wait_ld();
-      if (!full) {
-#pragma unroll
-        for (int i = 0; i < 32; ++i)
-          if (32 * c + i >= lim) u[i] = __float_as_uint(-INFINITY);
-      }
+    auto p_store = [&](const uint32_t (&u)[32], uint32_t col) {
       uint32_t uh[16], ul[16];
 #pragma unroll
       for (int i = 0; i < 16; ++i) {
@@ -366,81 +374,36 @@ __device__ __forceinline__ void softmax_role(const Params& p, unsigned char* sme
         ls = add2(ls, e);
         p_pair(e.x, e.y, uh[i], ul[i], (T*)nullptr);
       }
-      tc::tmem_st16(lane_base + scol + 32 * c, uh);
-      if constexpr (C::SPLIT) tc::tmem_st16(lane_base + scol + 32 * c + 16, ul);
-    }
-    const float lsum = ls.x + ls.y;
-    l += lsum;
+      tc::tmem_st16(lane_base + col, uh);
+      if constexpr (C::SPLIT) tc::tmem_st16(lane_base + col + 16, ul);
+    };
+    p_store(sa, scol);
+    p_store(sb2, scol + 32);
+    l += ls.x + ls.y;
     tc::tmem_wait_st();
     tc::fence_before_sync();
-    arrive_to_leader<PAIR>(&p_full[grp]);
-    last_j = j;
+    arrive_to_leader<PAIR>(&p_full[sb]);
   }
 
-  // epilogue: merge the two groups' (m, l, O) per row, O / l -> out.  Each
-  // warp of a pair writes half of the columns.  (m, l) cross through TMEM
-  // columns of this group's (now idle) S buffer.
-  const uint32_t xcol = grp ? C::COL_S1 : C::COL_S0;
-  const uint32_t xcol_other = grp ? C::COL_S0 : C::COL_S1;
-  float mo = -INFINITY, lo_ = 0.f;
-  bool have_mine = false, have_other = false;
-  if (ok) {
-    // all of this row's P V products must be complete: wait both groups' last
-    const int lj[2] = {n_tiles >= 1 ? ((n_tiles - 1) & ~1) : -1,
-                       n_tiles >= 2 ? (((n_tiles - 2) & ~1) | 1) : -1};
-    for (int g = 0; g < 2 && ok; ++g)
-      if (lj[g] >= 0 && !warp_wait_t<PAIR>(&o_ready[g], (lj[g] >> 1) & 1, abort_s)) ok = false;
-    have_mine = lj[grp] >= 0;
-    have_other = lj[grp ^ 1] >= 0;
-    (void)last_j;
-  }
-  if (ok) {
-    tc::fence_after_sync();
-    uint32_t x[32];
-    x[0] = __float_as_uint(m_ref);
-    x[1] = __float_as_uint(l);
-#pragma unroll
-    for (int i = 2; i < 32; ++i) x[i] = 0;
-    tc::tmem_st32(lane_base + xcol, x);
-    tc::tmem_wait_st();
-    tc::fence_before_sync();
-    mbar_arrive(&pair_bar[quad]);
-    if (warp_wait_t<false>(&pair_bar[quad], 0, abort_s)) {
-      tc::fence_after_sync();
-      uint32_t y[32];
-      tc::tmem_ld32(lane_base + xcol_other, y);
-      tc::tmem_wait_ld();
-      mo = __uint_as_float(y[0]);
-      lo_ = __uint_as_float(y[1]);
-    } else {
-      ok = false;
-    }
-  }
-  constexpr int HD = D / 2;
+  // epilogue: O / (l_0 + l_1) -> out, group g writing its HD columns
   float o[HD];
 #pragma unroll
   for (int i = 0; i < HD; ++i) o[i] = 0.f;
+  if (ok && n_tiles > 0 &&
+      !warp_wait_t<PAIR>(&o_ready[(n_tiles - 1) & 1], ((n_tiles - 1) >> 1) & 1, abort_s))
+    ok = false;
   if (ok) {
-    // this warp's output columns [grp * HD, grp * HD + HD) from both O buffers
-    const float mA = grp ? mo : m_ref, lA = grp ? lo_ : l;
-    const float mB = grp ? m_ref : mo, lB = grp ? l : lo_;
-    const bool hasA = grp ? have_other : have_mine, hasB = grp ? have_mine : have_other;
-    const float mm = fmaxf(hasA ? mA : -INFINITY, hasB ? mB : -INFINITY);
-    const float wA = (hasA && lA > 0.f) ? fast_exp2(mA - mm) : 0.f;
-    const float wB = (hasB && lB > 0.f) ? fast_exp2(mB - mm) : 0.f;
-    const float L = lA * wA + lB * wB;
-    const float inv = L > 0.f ? 1.f / L : 0.f;
+    const float L = l + exchange(l);
+    if (ok) {
+      const float inv = L > 0.f ? 1.f / L : 0.f;
+      tc::fence_after_sync();
 #pragma unroll
-    for (int c4 = 0; c4 < HD / 32; ++c4) {
-      uint32_t ua[32], ub[32];
-      tc::tmem_ld32(lane_base + C::COL_O + grp * HD + 32 * c4, ua);
-      tc::tmem_ld32(lane_base + C::COL_O + D + grp * HD + 32 * c4, ub);
-      tc::tmem_wait_ld();
+      for (int c4 = 0; c4 < HD / 32; ++c4) {
+        uint32_t u[32];
+        tc::tmem_ld32(lane_base + ocol + 32 * c4, u);
+        tc::tmem_wait_ld();
 #pragma unroll
-      for (int i = 0; i < 32; ++i) {
-        const float a = wA > 0.f ? __uint_as_float(ua[i]) * wA : 0.f;
-        const float bb = wB > 0.f ? __uint_as_float(ub[i]) * wB : 0.f;
-        o[32 * c4 + i] = (a + bb) * inv;
+        for (int i = 0; i < 32; ++i) o[32 * c4 + i] = n_tiles > 0 ? __uint_as_float(u[i]) * inv : 0.f;
       }
     }
   }

@@ -27,6 +27,7 @@ PA_ERR_CUDA = 8
 PA_ERR_TOO_LARGE = 9
 PA_ERR_NO_DEVICE = 10
 PA_DEVERR_BLOCK_ID, PA_DEVERR_CONTEXT, PA_DEVERR_TIMEOUT, PA_DEVERR_MERGE = 1, 2, 4, 8
+PA_DEVERR_RANGE = 0x10
 PA_IPC_HANDLE_BYTES = 64
 
 _P = ctypes.c_void_p

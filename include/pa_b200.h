@@ -87,6 +87,9 @@ typedef enum pa_status {
 #define PA_DEVERR_TIMEOUT 0x4    /* a bounded pipeline wait gave up           */
 #define PA_DEVERR_MERGE 0x8      /* a split-merge arrival never registered;
                                     its rows are NaN                           */
+#define PA_DEVERR_RANGE 0x10     /* tensor-core prefill on an fp16 pool: a
+                                    query element times scale is at or beyond
+                                    the fp16 range (|x| >= 65520)             */
 
 PA_API int pa_abi_version(void);
 
