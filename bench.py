@@ -760,13 +760,21 @@ def run_config4(torch, ops, harness, dev, stream, args) -> dict:
     peak = _peak_tflops()
     return {"value": round(tflops, 1), "unit": "TFLOP/s",
             "pct_of_measured_bf16_peak": round(100 * tflops / peak["bf16_tflops"], 1),
+            "pct_of_measured_bf16_sustained_peak": round(100 * tflops / peak["bf16_sustained"], 1)
+            if peak.get("bf16_sustained") else None,
             "peak_source": peak["src"], "ms_per_call": round(ms, 4), "flops_per_call": flops,
             "calls": n, "correctness_gate_max_abs": err,
-            "kernel": "pa::prefill::prefill_tc_kernel<__nv_bfloat16,128> (tcgen05, bf16 hi/lo)",
+            "tensor_pipe_active_pct": _profile_value("prefill_pair_config4", "tensor_pipe_active_pct"),
+            "tensor_pipe_source": "ncu sm__pipe_tensor_cycles_active, profiles/prefill_pair_config4.md",
+            "traffic_bytes_per_launch": _profile_traffic("prefill_pair_config4"),
+            "kernel": "pa::prefill::prefill_pair_kernel<__nv_bfloat16> (tcgen05 cta_group::2 "
+                      "CTA pairs, bf16 hi/lo)",
             "write_kv": {"value": round(wkv_bytes / (wkv_ms * 1e-3) / 1e9, 1), "unit": "GB/s",
                          "bytes": wkv_bytes, "ms": round(wkv_ms, 3),
                          "note": "4 sequences x 4096 tokens x 32 heads, fp32 device source, "
-                                 "through TorchBlockAllocator.write_kv, mean of 5 passes after one"}}
+                                 "through TorchBlockAllocator.write_kv, mean of 5 passes after one",
+                         "kernel_traffic_bytes_per_launch": _profile_traffic("write_kv_config4"),
+                         "traffic_source": "profiles/write_kv_config4.md (one sequence per launch)"}}
 
 
 def _peak_tflops() -> dict:
@@ -774,7 +782,9 @@ def _peak_tflops() -> dict:
     if p.exists():
         try:
             d = json.loads(p.read_text())
-            return {"bf16_tflops": float(d["bf16_tflops"]), "src": "measured (burst)"}
+            return {"bf16_tflops": float(d["bf16_tflops"]),
+                    "bf16_sustained": float(d.get("bf16_tflops_sustained", 0)) or None,
+                    "src": "measured (burst; sustained beside it)"}
         except (OSError, ValueError, KeyError):
             pass
     return {"bf16_tflops": 1590.0, "src": "fallback"}
