@@ -122,8 +122,9 @@ class ClockSampler:
     def __init__(self, gpu_index: int):
         self.idx = gpu_index
         self.proc = None
-        self.lines: list[str] = []
+        self.lines: list[tuple[float, str]] = []
         self.t = None
+        self.window = [0.0, None]
 
     def __enter__(self):
         try:
@@ -136,13 +137,15 @@ class ClockSampler:
             time.sleep(0.3)
         except (OSError, FileNotFoundError):
             self.proc = None
+        self.window = [time.monotonic(), None]
         return self
 
     def _read(self):
         for line in self.proc.stdout:
-            self.lines.append(line.strip())
+            self.lines.append((time.monotonic(), line.strip()))
 
     def __exit__(self, *exc):
+        self.window[1] = time.monotonic()
         if self.proc:
             self.proc.terminate()
             try:
@@ -155,7 +158,11 @@ class ClockSampler:
     def summary(self) -> dict:
         sm, mx, reasons = [], [], set()
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for line in self.lines:
+        # only the samples taken inside the `with` body (the start-up pre-roll is idle)
+        t0, t1 = self.window if self.window[1] is not None else (self.window[0], float("inf"))
+        for ts, line in self.lines:
+            if not t0 <= ts <= t1:
+                continue
             f = [x.strip() for x in line.split(",")]
             if len(f) < 9:
                 continue
@@ -747,13 +754,14 @@ def run_config4(torch, ops, harness, dev, stream, args) -> dict:
     for _ in range(args.warmup):
         call()
     torch.cuda.synchronize()
-    n = max(10, args.steps // 10)
+    n = max(250, args.steps // 2)  # ~0.35 s: long enough for a few dozen clock samples
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record(stream)
-    for _ in range(n):
-        call()
-    e1.record(stream)
-    torch.cuda.synchronize()
+    with ClockSampler(dev.index if dev.index is not None else 0) as clocks:
+        e0.record(stream)
+        for _ in range(n):
+            call()
+        e1.record(stream)
+        torch.cuda.synchronize()
     ms = e0.elapsed_time(e1) / n
     flops = harness.prefill_flops([S4] * B4, S4, H4, D4)
     tflops = flops / (ms * 1e-3) / 1e12
@@ -764,6 +772,7 @@ def run_config4(torch, ops, harness, dev, stream, args) -> dict:
             if peak.get("bf16_sustained") else None,
             "peak_source": peak["src"], "ms_per_call": round(ms, 4), "flops_per_call": flops,
             "calls": n, "correctness_gate_max_abs": err,
+            "clocks": clocks.summary(),
             "tensor_pipe_active_pct": _profile_value("prefill_pair_config4", "tensor_pipe_active_pct"),
             "tensor_pipe_source": "ncu sm__pipe_tensor_cycles_active, profiles/prefill_pair_config4.md",
             "traffic_bytes_per_launch": _profile_traffic("prefill_pair_config4"),

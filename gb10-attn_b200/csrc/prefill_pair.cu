@@ -1,30 +1,29 @@
 // prefill_pair.cu -- causal paged prefill for head_dim 128 on CTA pairs
-// sharing one tensor-core MMA (tcgen05 cta_group::2).
+// sharing one tensor-core MMA (tcgen05 cta_group::2), two chains per CTA.
 //
-// Same algorithm as prefill_tc.cu (S = Q K^T in tensor memory, softmax by two
-// ping-pong warpgroups that alternate over the KV tiles, P V with P read from
-// tensor memory, the causal rule of gb10-attn kernels/paged_attn_prefill.cu:
-// 62-65), laid out for two SMs:
+// Same algorithm as prefill_tc.cu (S = Q K^T in tensor memory, P written over
+// S and used as the A operand of P V, the causal rule of gb10-attn
+// kernels/paged_attn_prefill.cu:62-65), laid out for two SMs and two
+// independent row chains:
 //
-//   * A cluster of two CTAs takes 256 consecutive query rows of one (sequence,
-//     head): the even CTA ("leader") rows 0-127, the odd one rows 128-255.
-//     Each keeps its own Q (hi / lo parts for bf16 pools), S, P and O in its
-//     own shared and tensor memory, exactly as a CTA of prefill_tc.cu does.
-//   * The leader's MMA warp issues M = 256 MMAs for both CTAs.  The B operand
-//     is split between the CTAs by its N dimension: for S = Q K^T each CTA
-//     holds 64 of a tile's 128 keys (all 128 head-dim columns); for O += P V
-//     each CTA holds one 64-column half of V for all 128 keys.  So every K and
-//     V byte of a tile crosses from L2 into shared memory once per 256 query
-//     rows instead of once per 128, halving the tile traffic that limits
-//     prefill_tc.cu (its load-only variant takes 70 % of its run time).
-//   * Each CTA's TMA warp loads its halves; the K bytes of both CTAs count on
-//     the leader's k_full barrier, the V bytes on the leader's v_full (plus one
-//     arrival from the odd CTA after it wrote its rows past the context).
-//     The leader's commits arrive on the stage-free and S / O barriers of both
-//     CTAs.  The odd CTA's softmax threads arrive on the leader's q_ready and
-//     p_full barriers through their cluster addresses.
-//   * Loads are plain tiled TMA into the CTA's own shared memory: no cluster
-//     broadcast.
+//   * A cluster of two CTAs takes 512 consecutive query rows of one (sequence,
+//     head) as two chains of 256: chain c = rows 256 c .. 256 c + 255, of which
+//     the even CTA ("leader") holds rows 0-127 and the odd CTA rows 128-255.
+//     Each CTA keeps its two 128-row Q tiles, S tiles and O accumulators in its
+//     own shared and tensor memory (TMEM: S0, S1, O0, O1 = 512 columns).
+//   * The leader's MMA warp issues M = 256 MMAs for both CTAs, alternating the
+//     chains: P V of chain c on tile j, then S of chain c on tile j + 1, so one
+//     chain's MMAs run while the other chain's softmax works.  The B operand is
+//     split between the CTAs by its N dimension: for S = Q K^T each CTA holds 64
+//     of a tile's 128 keys, for O += P V one 64-column half of V; each K and V
+//     tile serves all 512 rows.
+//   * Softmax: warpgroup c of each CTA owns chain c (one thread per row, the
+//     whole 128-key row; prefill_tc.cuh softmax_chain).
+//   * Loads: warp 9 K, warp 10 V, plain tiled TMA into the CTA's own shared
+//     memory (no cluster broadcast); the odd CTA's bytes count on the leader's
+//     barriers through the pair form of the load.  The leader's commits arrive
+//     on both CTAs' barriers; the odd CTA's softmax threads arrive on the
+//     leader's q_ready and p_full barriers through their cluster addresses.
 //
 // Every wait is bounded (PA_DEVERR_TIMEOUT), and both CTAs meet at a cluster
 // barrier before freeing the pair's tensor memory, so neither leaves while
@@ -44,35 +43,35 @@ template <typename T>
 struct PairCfg {
   static constexpr int D = 128;
   static constexpr bool SPLIT = Fmt<T>::split;
-  static constexpr uint32_t Q_BYTES = BM * D * 2;       // one Q part: 2 halves x 128 rows x 128 B
+  static constexpr uint32_t Q_PART = BM * D * 2;        // one Q part: 2 halves x 128 rows x 128 B
+  static constexpr uint32_t Q_CHAIN = Q_PART * (SPLIT ? 2 : 1);
   static constexpr int KROWS = BN / 2;                  // keys of a K tile per CTA
   static constexpr uint32_t K_BYTES = KROWS * D * 2;    // 2 halves x 64 rows x 128 B
   static constexpr uint32_t V_BYTES = BN * 64 * 2;      // 128 rows x 128 B (one half)
   static constexpr uint32_t GROUP_BYTES = 16 * 128;     // one TMA box: 16 rows x 128 B
-  static constexpr int NK = 5;
-  static constexpr int NV = 4;
-  static constexpr uint32_t OFF_QH = 0;
-  static constexpr uint32_t OFF_QL = Q_BYTES;
-  static constexpr uint32_t OFF_K = Q_BYTES * (SPLIT ? 2 : 1);
+  // each K / V tile serves both chains, so the rings turn at half the rate
+  static constexpr int NK = SPLIT ? 3 : 5;
+  static constexpr int NV = SPLIT ? 2 : 4;
+  static constexpr uint32_t OFF_Q = 0;                  // [chain][hi, lo]
+  static constexpr uint32_t OFF_K = 2 * Q_CHAIN;
   static constexpr uint32_t OFF_V = OFF_K + NK * K_BYTES;
   static constexpr uint32_t OFF_BAR = OFF_V + NV * V_BYTES;
-  // K and V full / empty rings, s_full / p_full / o_ready pairs, q_ready, 4
-  // pair barriers; then the TMEM address and the abort flag
-  static constexpr uint32_t N_BARS = 2 * NK + 2 * NV + 2 * 3 + 1 + 4;
+  // K and V full / empty rings, per-chain s_full / p_full / o_ready, q_ready;
+  // then the TMEM address and the abort flag
+  static constexpr uint32_t N_BARS = 2 * NK + 2 * NV + 2 * 3 + 1;
   static constexpr uint32_t OFF_BT = OFF_BAR + ((N_BARS * 8 + 8 + 15) / 16) * 16;
   // two block-id chunks: one per loading warp (K, V)
-  static constexpr uint32_t OFF_XCH = OFF_BT + 2 * kBtChunk * 4;    // [2][2][128] fp32
-  static constexpr uint32_t SMEM = OFF_XCH + 2048 + 1024;            // + alignment slack
+  static constexpr uint32_t SMEM = OFF_BT + 2 * kBtChunk * 4 + 1024;  // + alignment slack
   static_assert(SMEM <= 227 * 1024, "shared memory budget");
-  // TMEM columns: S buffers at 0 and 128 (tiles j % 2), O at 256
-  static constexpr uint32_t COL_S0 = 0, COL_S1 = 128, COL_O = 256;
+  // TMEM columns: S of chain c at 128 c, O of chain c at 256 + D c
+  static constexpr uint32_t COL_S0 = 0, COL_O = 256;
 };
 
 constexpr uint16_t kBoth = 0x3;  // CTA mask of the pair for commits
 
 }  // namespace
 
-// Grid: 2 CTAs per 256 query rows of one (sequence, head), clusters of 2.
+// Grid: 2 CTAs per 512 query rows of one (sequence, head), clusters of 2.
 template <typename T>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     prefill_pair_kernel(const __grid_constant__ Params p) {
@@ -82,30 +81,28 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
   unsigned char* smem = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::OFF_BAR);
   uint64_t* k_full = bars;            // [NK] leader: both CTAs' K halves landed
-  uint64_t* k_empty = k_full + NK;    // [NK] S = Q K^T done with the stage (both CTAs)
+  uint64_t* k_empty = k_full + NK;    // [NK] both chains' S = Q K^T done with the stage
   uint64_t* v_full = k_empty + NK;    // [NV] leader: both V halves landed / written
-  uint64_t* v_empty = v_full + NV;    // [NV] P V done with the stage (both CTAs)
-  uint64_t* s_full = v_empty + NV;    // [2] S of tile j in tensor memory (both CTAs)
-  uint64_t* p_full = s_full + 2;      // [2] leader: P of tile j written in both CTAs
-  uint64_t* o_ready = p_full + 2;     // [2] P V of tile j done (both CTAs)
-  uint64_t* q_ready = o_ready + 2;    // leader: Q of both CTAs staged
-  uint64_t* pair_bar = q_ready + 1;   // [4] row max / sum exchange inside the CTA
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(pair_bar + 4);
+  uint64_t* v_empty = v_full + NV;    // [NV] both chains' P V done with the stage
+  uint64_t* s_full = v_empty + NV;    // [2] chain c: S tile in tensor memory (both CTAs)
+  uint64_t* p_full = s_full + 2;      // [2] leader, chain c: P written in both CTAs
+  uint64_t* o_ready = p_full + 2;     // [2] chain c: P V of its latest tile done (both CTAs)
+  uint64_t* q_ready = o_ready + 2;    // leader: Q of both chains of both CTAs staged
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(q_ready + 1);
   int32_t* abort_s = reinterpret_cast<int32_t*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const uint32_t rank = tc::cluster_ctarank();  // 0: leader (rows 0-127 of the pair)
+  const uint32_t rank = tc::cluster_ctarank();  // 0: leader
 
-  // Consecutive pairs take the 256-row tiles of one (sequence, head), longest
-  // first (as prefill_tc.cu), so the pairs resident together share its K/V in L2.
+  // Consecutive pairs take the 512-row items of one (sequence, head),
+  // longest first, so the pairs resident together share its K/V in L2.
   const int64_t c = blockIdx.x >> 1;
-  const int n_pairs = (p.n_qtiles + 1) / 2;
-  const int pt = n_pairs - 1 - (int)(c % n_pairs);
-  const int64_t bh = c / n_pairs;
+  const int n_items = (p.n_qtiles + 3) / 4;
+  const int it = n_items - 1 - (int)(c % n_items);
+  const int64_t bh = c / n_items;
   const int64_t b = bh / p.H, h = bh % p.H;
   const int64_t kv_h = h / (p.H / p.HKV);
-  const int64_t pq0 = (int64_t)pt * 2 * BM;      // the pair's first query row
-  const int64_t q0 = pq0 + (int64_t)rank * BM;   // this CTA's
+  const int64_t item0 = (int64_t)it * 4 * BM;  // the item's first query row
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < NK; ++s) {
@@ -118,11 +115,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     }
     for (int s = 0; s < 2; ++s) {
       mbar_init(&s_full[s], 1);
-      mbar_init(&p_full[s], 2 * kSoftmaxWarps * 32);  // both warpgroups of both CTAs
+      mbar_init(&p_full[s], 2 * 4 * 32);  // chain s's warpgroup in both CTAs
       mbar_init(&o_ready[s], 1);
     }
     mbar_init(q_ready, 2 * kSoftmaxWarps * 32);
-    for (int qd = 0; qd < 4; ++qd) mbar_init(&pair_bar[qd], 64);
     *abort_s = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
@@ -136,28 +132,31 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
   tc::fence_after_sync();
   const uint32_t tmem = *tmem_slot;
 
-  // keys the pair's query rows need: [0, min(ctx, ctx - Sq + last row + 1))
   int64_t ctx = p.context_lens[b];
   const int64_t max_ctx = p.MB * p.BS;
   if (ctx > max_ctx) {
     if (threadIdx.x == 0 && rank == 0) report(p.dev_status, PA_DEVERR_CONTEXT);
     ctx = max_ctx;
   }
-  const int64_t q_last = min(pq0 + 2 * BM, p.Sq) - 1;
-  const int64_t key_end = min(ctx, ctx - p.Sq + q_last + 1);
-  const int n_tiles = key_end > 0 ? (int)((key_end + BN - 1) / BN) : 0;
-  // The pairs of one head run side by side and share its K/V in L2; each
-  // starts its walk over the KV tiles at a different tile, so they do not all
-  // request the same lines at the same moment.
-  const int rot = n_tiles > 0 ? (int)((c * 7) % n_tiles) : 0;
-  auto phys = [&](int j) { return j + rot < n_tiles ? j + rot : j + rot - n_tiles; };
+  // KV tiles chain k needs: keys [0, min(ctx, ctx - Sq + its last row + 1))
+  int ntile[2];
+#pragma unroll
+  for (int k = 0; k < 2; ++k) {
+    const int64_t first = item0 + 2 * BM * k;
+    const int64_t last = min(first + 2 * BM, p.Sq) - 1;
+    const int64_t key_end = min(ctx, ctx - p.Sq + last + 1);
+    ntile[k] = (first < p.Sq && key_end > 0) ? (int)((key_end + BN - 1) / BN) : 0;
+  }
+  const int n_tiles = max(ntile[0], ntile[1]);  // tiles loaded
+  // the chain that uses tile j last (its S / P V releases the K / V stage)
+  auto last_user = [&](int j) { return j < ntile[1] ? 1 : 0; };
+  auto phys = [&](int j) { return j; };
 
   if (warp < kSoftmaxWarps) {
     asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kSoftmaxRegs));
-    softmax_role<T, D, C, true>(p, smem, tmem,
-                                Bars{s_full, p_full, o_ready, q_ready, pair_bar,
-                                     reinterpret_cast<float*>(smem + C::OFF_XCH)},
-                                abort_s, warp, lane, b, h, q0, ctx, n_tiles, rot);
+    const int grp = warp >> 2;
+    softmax_chain<T, D, C>(p, smem, tmem, s_full, p_full, o_ready, q_ready, abort_s, warp, lane,
+                           grp, b, h, item0 + 2 * BM * grp + (int64_t)rank * BM, ctx, ntile[grp]);
   } else {
    asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kOtherRegs));
    if (warp == kMmaWarp) {
@@ -165,51 +164,66 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     if (rank == 0 && lane == 0 && n_tiles > 0) {
       constexpr uint32_t idesc_s = tc::idesc_f16(Fmt<T>::id, 2 * BM, BN, false);
       constexpr uint32_t idesc_o = tc::idesc_f16(Fmt<T>::id, 2 * BM, D, true);
-      const uint32_t qh = smem_u32(smem + C::OFF_QH), ql = smem_u32(smem + C::OFF_QL);
       bool ok = mbar_wait_cl(q_ready, 0, abort_s);
       tc::fence_after_sync();
-      auto issue_s = [&](int jj) -> bool {
+      int k_seen = -1, v_seen = -1;  // latest K / V tile waited for
+      auto issue_s = [&](int k, int jj) -> bool {
         const int st = jj % NK;
-        if (!mbar_wait_cl(&k_full[st], (jj / NK) & 1, abort_s)) return false;
-        tc::fence_after_sync();
-        const uint32_t kb = smem_u32(smem + C::OFF_K + st * C::K_BYTES);
-        const uint32_t dcol = tmem + ((jj & 1) ? C::COL_S1 : C::COL_S0);
-#pragma unroll
+        if (jj > k_seen) {
+          if (!mbar_wait_cl(&k_full[st], (jj / NK) & 1, abort_s)) return false;
+          tc::fence_after_sync();
+          k_seen = jj;
+        }
+        // descriptors: base + (byte offset >> 4) in the start-address field
+        // (shared-memory offsets stay below 2^18 bytes, so no carry)
+        const uint64_t kd = tc::smem_desc_sw128(smem_u32(smem + C::OFF_K + st * C::K_BYTES), 16, 1024);
+        const uint64_t qd0 = tc::smem_desc_sw128(smem_u32(smem + C::OFF_Q + k * C::Q_CHAIN), 16, 1024);
+        const uint32_t dcol = tmem + C::COL_S0 + 128 * k;
+#pragma unroll 1
         for (int part = 0; part < (C::SPLIT ? 2 : 1); ++part) {
-          const uint32_t qb = part ? ql : qh;
+          const uint64_t qd = qd0 + (uint64_t)((part * C::Q_PART) >> 4);
 #pragma unroll
           for (int kk = 0; kk < D / 16; ++kk) {
             const uint32_t koff = (kk >> 2) * (C::KROWS * 128) + (kk & 3) * 32;
             const uint32_t qoff = (kk >> 2) * (BM * 128) + (kk & 3) * 32;
-            tc::mma_ss_pair(dcol, tc::smem_desc_sw128(qb + qoff, 16, 1024),
-                            tc::smem_desc_sw128(kb + koff, 16, 1024), idesc_s, (part | kk) != 0);
+            tc::mma_ss_pair(dcol, qd + (qoff >> 4), kd + (koff >> 4), idesc_s, (part | kk) != 0);
           }
         }
-        tc::mma_commit_pair(&s_full[jj & 1], kBoth);
-        tc::mma_commit_pair(&k_empty[st], kBoth);
+        tc::mma_commit_pair(&s_full[k], kBoth);
+        if (last_user(jj) == k) tc::mma_commit_pair(&k_empty[st], kBoth);
         return true;
       };
-      if (ok) ok = issue_s(0);
+      for (int k = 0; k < 2 && ok; ++k)
+        if (ntile[k] > 0) ok = issue_s(k, 0);
       for (int j = 0; j < n_tiles && ok; ++j) {
-        if (j + 1 < n_tiles && !issue_s(j + 1)) { ok = false; break; }
-        if (!mbar_wait_cl(&p_full[j & 1], (j >> 1) & 1, abort_s)) { ok = false; break; }
-        const int vs = j % NV;
-        if (!mbar_wait_cl(&v_full[vs], (j / NV) & 1, abort_s)) { ok = false; break; }
-        tc::fence_after_sync();
-        const uint32_t vb = smem_u32(smem + C::OFF_V + vs * C::V_BYTES);
-        const uint32_t pcol = tmem + ((j & 1) ? C::COL_S1 : C::COL_S0);
-#pragma unroll
-        for (int part = 0; part < (C::SPLIT ? 2 : 1); ++part) {
-#pragma unroll
-          for (int kk = 0; kk < BN / 16; ++kk) {
-            // keys 16kk .. 16kk + 15: 8 columns of packed pairs
-            tc::mma_ts_pair(tmem + C::COL_O, pcol + (kk >> 1) * 32 + (kk & 1) * 8 + part * 16,
-                            tc::smem_desc_sw128(vb + kk * 16 * 128, BN * 128, 1024), idesc_o,
-                            (j > 0 || part > 0 || kk > 0) ? 1u : 0u);
+        for (int k = 0; k < 2 && ok; ++k) {
+          if (j >= ntile[k]) continue;
+          if (!mbar_wait_cl(&p_full[k], j & 1, abort_s)) { ok = false; break; }
+          const int vs = j % NV;
+          if (j > v_seen) {
+            if (!mbar_wait_cl(&v_full[vs], (j / NV) & 1, abort_s)) { ok = false; break; }
+            v_seen = j;
           }
+          tc::fence_after_sync();
+          const uint64_t vd = tc::smem_desc_sw128(smem_u32(smem + C::OFF_V + vs * C::V_BYTES),
+                                                  BN * 128, 1024);
+          const uint32_t pcol = tmem + C::COL_S0 + 128 * k;
+#pragma unroll 1
+          for (int part = 0; part < (C::SPLIT ? 2 : 1); ++part) {
+#pragma unroll
+            for (int kk = 0; kk < BN / 16; ++kk) {
+              // keys 16kk .. 16kk + 15: 8 columns of packed pairs
+              tc::mma_ts_pair(tmem + C::COL_O + D * k,
+                              pcol + (kk >> 1) * 32 + (kk & 1) * 8 + part * 16,
+                              vd + (uint64_t)((kk * 16 * 128) >> 4), idesc_o,
+                              (j > 0 || part > 0 || kk > 0) ? 1u : 0u);
+            }
+          }
+          tc::mma_commit_pair(&o_ready[k], kBoth);
+          if (last_user(j) == k) tc::mma_commit_pair(&v_empty[vs], kBoth);
+          // the chain's next S overwrites its P: issued after its P V, in order
+          if (j + 1 < ntile[k]) ok = issue_s(k, j + 1);
         }
-        tc::mma_commit_pair(&v_empty[vs], kBoth);
-        tc::mma_commit_pair(&o_ready[j & 1], kBoth);
       }
       if (!ok) report(p.dev_status, PA_DEVERR_TIMEOUT);
     }
@@ -334,11 +348,11 @@ static int launch_pair_typed(const Params& p, int64_t grid, cudaStream_t s) {
 }
 
 // Launches the pair kernel for a head_dim 128 fp16 / bf16 pool (the caller
-// built `p` and checked eligibility); one cluster of two CTAs per 256 query
+// built `p` and checked eligibility); one cluster of two CTAs per 512 query
 // rows of each (sequence, head).
 int launch_pair(const Params& p, int dtype, cudaStream_t s) {
-  const int64_t n_pairs = (p.n_qtiles + 1) / 2;
-  const int64_t grid = 2 * n_pairs * p.B * p.H;
+  const int64_t n_items = (p.n_qtiles + 3) / 4;
+  const int64_t grid = 2 * n_items * p.B * p.H;
   if (grid <= 0) return PA_OK;
   if (grid > (int64_t(1) << 31) - 1) return PA_ERR_TOO_LARGE;
   return dtype == PA_DTYPE_BF16 ? launch_pair_typed<__nv_bfloat16>(p, grid, s)

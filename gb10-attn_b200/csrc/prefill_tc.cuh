@@ -14,15 +14,16 @@ namespace prefill {
 
 constexpr int BM = 128;  // query rows per CTA
 constexpr int BN = 128;  // keys per KV tile
-// Warpgroups 0-1: softmax (warpgroup g takes the KV tiles j % 2 == g);
-// warpgroup 2: warp 8 issues the MMAs, warp 9 the TMA loads, warps 10-11 idle.
+// Warpgroups 0-1: softmax (the 1-SM kernel splits each score tile's columns
+// between them; the pair kernel gives each its own chain of query rows);
+// warpgroup 2: warp 8 issues the MMAs, warps 9-10 the TMA loads.
 // Registers: 384 threads launched at 168 (64512); setmaxnreg gives the
-// softmax warpgroups 232 and the rest 40: 256 x 232 + 128 x 40 = 64512.
+// softmax warpgroups 224 and the rest 56: 256 x 224 + 128 x 56 = 64512.
 constexpr int kSoftmaxWarps = 8;
 constexpr int kMmaWarp = 8;
 constexpr int kTmaWarp = 9;
 constexpr int kThreads = 384;
-constexpr int kSoftmaxRegs = 232, kOtherRegs = 40;
+constexpr int kSoftmaxRegs = 224, kOtherRegs = 56;
 static_assert(256 * kSoftmaxRegs + 128 * kOtherRegs <= kThreads * 168, "register split");
 constexpr uint32_t kTmemCols = 512;
 // block ids the TMA warp stages in shared memory per refill (32 tiles at 16-token pages)
@@ -201,6 +202,51 @@ __device__ __forceinline__ void arrive_to_leader(uint64_t* bar) {
     mbar_arrive(bar);
 }
 
+// Q rows r0 .. r0 + 15 of the 128-row tile starting at query row q0 (sequence
+// b, head h) -> shared memory at qh (and the lo parts at ql for bf16 pools):
+// pre-scaled by scale * log2(e), 128-byte swizzled.  One warp; every row's
+// global load is issued before the first shared store, so the warp waits on
+// global memory once.  Returns true if a scaled element is outside the fp16
+// range and Q is kept as one fp16 part.
+template <typename T, int D, typename C>
+__device__ __forceinline__ bool stage_q(const Params& p, unsigned char* qh, unsigned char* ql,
+                                        int64_t b, int64_t h, int64_t q0, int r0, int lane) {
+  constexpr int EPT = D / 32;  // elements per lane per row
+  constexpr int RPW = 16;
+  float x[RPW][EPT];
+#pragma unroll
+  for (int i = 0; i < RPW; ++i) {
+    const int64_t qr = q0 + r0 + i;
+    const float* src = p.q + ((b * p.Sq + qr) * p.H + h) * D + lane * EPT;
+    if constexpr (EPT == 4) {
+      const float4 v = qr < p.Sq ? __ldg(reinterpret_cast<const float4*>(src)) : make_float4(0.f, 0.f, 0.f, 0.f);
+      x[i][0] = v.x, x[i][1] = v.y, x[i][2] = v.z, x[i][3] = v.w;
+    } else {
+#pragma unroll
+      for (int e = 0; e < EPT; e += 2) {
+        const float2 v = qr < p.Sq ? __ldg(reinterpret_cast<const float2*>(src + e)) : make_float2(0.f, 0.f);
+        x[i][e] = v.x, x[i][e + 1] = v.y;
+      }
+    }
+  }
+  bool qover = false;
+#pragma unroll
+  for (int i = 0; i < RPW; ++i) {
+    const int rr = r0 + i;
+#pragma unroll
+    for (int e = 0; e < EPT; e += 2) {
+      const uint32_t off = sw128_offset(rr, lane * EPT + e, BM);
+      uint32_t hi, lo;
+      const float a = x[i][e] * p.qscale, bq = x[i][e + 1] * p.qscale;
+      if constexpr (!C::SPLIT) qover |= !(fabsf(a) < 65520.f && fabsf(bq) < 65520.f);
+      split_pair(a, bq, hi, lo, (T*)nullptr);
+      *reinterpret_cast<uint32_t*>(qh + off) = hi;
+      if constexpr (C::SPLIT) *reinterpret_cast<uint32_t*>(ql + off) = lo;
+    }
+  }
+  return qover;
+}
+
 // The softmax role of both tensor-core prefill kernels: warps 0-7 of a CTA,
 // 128 query rows (rows q0 .. q0 + 127 of sequence b, head h) against the
 // n_tiles KV tiles of 128 keys.  Stages Q (pre-scaled, hi / lo parts) in
@@ -230,43 +276,8 @@ __device__ __forceinline__ void softmax_role(const Params& p, unsigned char* sme
   // Q tile -> shared memory, pre-scaled, hi (+ lo) parts, swizzled: warp w
   // converts rows 16w .. 16w+15.
   {
-    unsigned char* qh = smem + C::OFF_QH;
-    unsigned char* ql = smem + C::OFF_QL;
-    constexpr int EPT = D / 32;  // elements per lane per row
-    constexpr int RPW = BM / kSoftmaxWarps;  // rows per warp
-    // every row's global load is issued before the first shared store, so
-    // the warp waits on global memory once
-    float x[RPW][EPT];
-#pragma unroll
-    for (int i = 0; i < RPW; ++i) {
-      const int64_t qr = q0 + warp * RPW + i;
-      const float* src = p.q + ((b * p.Sq + qr) * p.H + h) * D + lane * EPT;
-      if constexpr (EPT == 4) {
-        const float4 v = qr < p.Sq ? __ldg(reinterpret_cast<const float4*>(src)) : make_float4(0.f, 0.f, 0.f, 0.f);
-        x[i][0] = v.x, x[i][1] = v.y, x[i][2] = v.z, x[i][3] = v.w;
-      } else {
-#pragma unroll
-        for (int e = 0; e < EPT; e += 2) {
-          const float2 v = qr < p.Sq ? __ldg(reinterpret_cast<const float2*>(src + e)) : make_float2(0.f, 0.f);
-          x[i][e] = v.x, x[i][e + 1] = v.y;
-        }
-      }
-    }
-    bool qover = false;  // fp16 pools: a scaled q element outside the fp16 range
-#pragma unroll
-    for (int i = 0; i < RPW; ++i) {
-      const int rr = warp * RPW + i;
-#pragma unroll
-      for (int e = 0; e < EPT; e += 2) {
-        const uint32_t off = sw128_offset(rr, lane * EPT + e, BM);
-        uint32_t hi, lo;
-        const float a = x[i][e] * p.qscale, bq = x[i][e + 1] * p.qscale;
-        if constexpr (!C::SPLIT) qover |= !(fabsf(a) < 65520.f && fabsf(bq) < 65520.f);
-        split_pair(a, bq, hi, lo, (T*)nullptr);
-        *reinterpret_cast<uint32_t*>(qh + off) = hi;
-        if constexpr (C::SPLIT) *reinterpret_cast<uint32_t*>(ql + off) = lo;
-      }
-    }
+    const bool qover = stage_q<T, D, C>(p, smem + C::OFF_QH, smem + C::OFF_QL, b, h, q0,
+                                        warp * 16, lane);
     if (qover) report(p.dev_status, PA_DEVERR_RANGE);
     tc::fence_proxy_async_smem();
     arrive_to_leader<PAIR>(q_ready);
@@ -412,6 +423,159 @@ __device__ __forceinline__ void softmax_role(const Params& p, unsigned char* sme
 #pragma unroll
     for (int i = 0; i < HD; i += 4)
       *reinterpret_cast<float4*>(dst + i) = make_float4(o[i], o[i + 1], o[i + 2], o[i + 3]);
+  }
+  if (!ok && lane == 0) report(p.dev_status, PA_DEVERR_TIMEOUT);
+}
+
+// The softmax role of the two-chain CTA-pair prefill (prefill_pair.cu).
+// Warpgroup `grp` owns one chain: the 128 query rows q0 .. q0 + 127 of this
+// CTA, one thread per row (TMEM lane), the whole 128-key row of each of the
+// chain's n_tiles S tiles (S at COL_S0 + 128 grp, O at COL_O + D grp), KV
+// tiles in order.  The other warpgroup runs the other chain on other rows, so
+// one chain's exponentials overlap the other's MMAs and no row statistic
+// crosses warps.  Stages its Q (pre-scaled, hi / lo parts) and writes O / l to
+// `out`.  Arrivals go to the leader CTA of the pair.
+template <typename T, int D, typename C>
+__device__ __forceinline__ void softmax_chain(const Params& p, unsigned char* smem, uint32_t tmem,
+                                              uint64_t* s_full, uint64_t* p_full,
+                                              uint64_t* o_ready, uint64_t* q_ready,
+                                              int32_t* abort_s, int warp, int lane, int grp,
+                                              int64_t b, int64_t h, int64_t q0, int64_t ctx,
+                                              int n_tiles) {
+  const int quad = warp & 3;
+  const int r = quad * 32 + lane;  // query row in the tile = TMEM lane
+  const int64_t qrow = q0 + r;
+  const bool row_valid = qrow < p.Sq;
+  const int64_t q_abs = ctx - p.Sq + qrow;  // absolute position of this query
+  {
+    unsigned char* qh = smem + C::OFF_Q + grp * C::Q_CHAIN;
+    unsigned char* ql = qh + C::Q_PART;
+    bool qover = stage_q<T, D, C>(p, qh, ql, b, h, q0, quad * 32, lane);
+    qover |= stage_q<T, D, C>(p, qh, ql, b, h, q0, quad * 32 + 16, lane);
+    if (qover) report(p.dev_status, PA_DEVERR_RANGE);
+    tc::fence_proxy_async_smem();
+    arrive_to_leader<true>(q_ready);
+  }
+  const uint32_t lane_base = tmem + ((uint32_t)(quad * 32) << 16);
+  const uint32_t scol = C::COL_S0 + 128 * grp;
+  const uint32_t ocol = C::COL_O + D * grp;
+  float m_ref = -INFINITY, l = 0.f;
+  bool ok = true;
+  for (int j = 0; j < n_tiles && ok; ++j) {
+    if (!warp_wait_t<true>(&s_full[grp], j & 1, abort_s)) { ok = false; break; }
+    tc::fence_after_sync();
+    // causal rule + context bound (kernels/paged_attn_prefill.cu:62-65):
+    // keys k0 + c of this tile are visible when c < lim
+    const int64_t k0 = (int64_t)j * BN;
+    const int64_t vis = row_valid ? min(q_abs + 1, ctx) - k0 : 0;
+    const int lim = vis <= 0 ? 0 : (vis >= BN ? BN : (int)vis);
+    // pass 1: row max over the visible keys (S streamed from TMEM, 32
+    // columns at a time); tiles with every key visible to all of the warp's
+    // rows skip the per-key mask
+    const bool full = __all_sync(0xffffffffu, lim == BN);
+    float mt = -INFINITY;
+    if (full) {
+      float m4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+#pragma unroll
+      for (int c4 = 0; c4 < BN / 32; ++c4) {
+        uint32_t u[32];
+        tc::tmem_ld32(lane_base + scol + 32 * c4, u);
+        tc::tmem_wait_ld();
+#pragma unroll
+        for (int i = 0; i < 32; ++i) m4[i & 3] = fmaxf(m4[i & 3], __uint_as_float(u[i]));
+      }
+      mt = fmaxf(fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3]));
+    } else {
+#pragma unroll
+      for (int c4 = 0; c4 < BN / 32; ++c4) {
+        uint32_t u[32];
+        tc::tmem_ld32(lane_base + scol + 32 * c4, u);
+        tc::tmem_wait_ld();
+#pragma unroll
+        for (int i = 0; i < 32; ++i)
+          if (32 * c4 + i < lim) mt = fmaxf(mt, __uint_as_float(u[i]));
+      }
+    }
+    // The reference max of a row moves only when the row's max grows by more
+    // than 2^8 (then O and l are rescaled, factor 1 for rows that keep theirs;
+    // tcgen05.ld/st are warp-collective).
+    const bool need = mt > m_ref + 8.f;
+    const float factor = need ? fast_exp2(m_ref - mt) : 1.f;  // 0 on a row's first visible tile
+    if (__any_sync(0xffffffffu, need) && j >= 1) {
+      // the chain's previous P V must have finished
+      if (!warp_wait_t<true>(&o_ready[grp], (j - 1) & 1, abort_s)) { ok = false; break; }
+      tc::fence_after_sync();
+#pragma unroll
+      for (int c4 = 0; c4 < D / 32; ++c4) {
+        uint32_t u[32];
+        tc::tmem_ld32(lane_base + ocol + 32 * c4, u);
+        tc::tmem_wait_ld();
+#pragma unroll
+        for (int i = 0; i < 32; ++i) u[i] = __float_as_uint(__uint_as_float(u[i]) * factor);
+        tc::tmem_st32(lane_base + ocol + 32 * c4, u);
+      }
+      tc::tmem_wait_st();
+    }
+    if (need) {
+      l *= factor;
+      m_ref = mt;
+    }
+    // pass 2: P = exp2(s - m_ref) into the S columns, 32 keys at a time (S
+    // re-read from TMEM): keys 32c .. 32c + 31 go to columns [32c, 32c + 16)
+    // as 16-bit pairs, their lo parts to [32c + 16, 32c + 32); every store
+    // lands on columns this pass has already read.  Masked keys get s = -inf.
+    // (a row with no visible key so far has m_ref = -inf and only masked keys here)
+    const float mneg = m_ref == -INFINITY ? 0.f : -m_ref;
+    const float2 negm = make_float2(mneg, mneg);
+    float2 ls = make_float2(0.f, 0.f);
+#pragma unroll
+    for (int c = 0; c < BN / 32; ++c) {
+      uint32_t u[32];
+      tc::tmem_ld32(lane_base + scol + 32 * c, u);
+      tc::tmem_wait_ld();
+      if (!full) {
+#pragma unroll
+        for (int i = 0; i < 32; ++i)
+          if (32 * c + i >= lim) u[i] = __float_as_uint(-INFINITY);
+      }
+      uint32_t uh[16], ul[16];
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {
+        const float2 x = add2(make_float2(__uint_as_float(u[2 * i]), __uint_as_float(u[2 * i + 1])), negm);
+        const float2 e = make_float2(fast_exp2(x.x), fast_exp2(x.y));
+        ls = add2(ls, e);
+        p_pair(e.x, e.y, uh[i], ul[i], (T*)nullptr);
+      }
+      tc::tmem_st16(lane_base + scol + 32 * c, uh);
+      if constexpr (C::SPLIT) tc::tmem_st16(lane_base + scol + 32 * c + 16, ul);
+    }
+    l += ls.x + ls.y;
+    tc::tmem_wait_st();
+    tc::fence_before_sync();
+    arrive_to_leader<true>(&p_full[grp]);
+  }
+
+  // epilogue: O / l -> out, 32 columns at a time
+  if (ok && n_tiles > 0 && !warp_wait_t<true>(&o_ready[grp], (n_tiles - 1) & 1, abort_s)) ok = false;
+  const bool have = ok && n_tiles > 0;
+  const float inv = l > 0.f ? 1.f / l : 0.f;
+  if (have) tc::fence_after_sync();
+  float* dst = p.out + ((b * p.Sq + qrow) * p.H + h) * D;
+#pragma unroll
+  for (int c4 = 0; c4 < D / 32; ++c4) {
+    uint32_t u[32];
+    if (have) {
+      tc::tmem_ld32(lane_base + ocol + 32 * c4, u);
+      tc::tmem_wait_ld();
+    }
+    if (row_valid) {
+#pragma unroll
+      for (int i = 0; i < 32; i += 4)
+        *reinterpret_cast<float4*>(dst + 32 * c4 + i) =
+            have ? make_float4(__uint_as_float(u[i]) * inv, __uint_as_float(u[i + 1]) * inv,
+                               __uint_as_float(u[i + 2]) * inv, __uint_as_float(u[i + 3]) * inv)
+                 : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
   }
   if (!ok && lane == 0) report(p.dev_status, PA_DEVERR_TIMEOUT);
 }
