@@ -115,7 +115,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     }
     for (int s = 0; s < 2; ++s) {
       mbar_init(&s_full[s], 1);
-      mbar_init(&p_full[s], 2 * 4 * 32);  // chain s's warpgroup in both CTAs
+      mbar_init(&p_full[s], 2 * 4);  // chain s: one arrival per warp of its warpgroup, both CTAs
       mbar_init(&o_ready[s], 1);
     }
     mbar_init(q_ready, 2 * kSoftmaxWarps * 32);

@@ -469,79 +469,52 @@ __device__ __forceinline__ void softmax_chain(const Params& p, unsigned char* sm
     const int64_t k0 = (int64_t)j * BN;
     const int64_t vis = row_valid ? min(q_abs + 1, ctx) - k0 : 0;
     const int lim = vis <= 0 ? 0 : (vis >= BN ? BN : (int)vis);
-    // pass 1: row max over the visible keys (S streamed from TMEM, 32
-    // columns at a time); tiles with every key visible to all of the warp's
-    // rows skip the per-key mask
+    // the row's 128 scores, read from TMEM once (four loads, one wait);
+    // masked keys become -inf, so the row max covers the visible keys only
     const bool full = __all_sync(0xffffffffu, lim == BN);
-    float mt = -INFINITY;
-    if (full) {
+    uint32_t u[BN];
+#pragma unroll
+    for (int c4 = 0; c4 < BN / 32; ++c4)
+      tc::tmem_ld32(lane_base + scol + 32 * c4, *reinterpret_cast<uint32_t(*)[32]>(u + 32 * c4));
+    tc::tmem_wait_ld();
+#pragma unroll
+    for (int c4 = 0; c4 < BN / 32; ++c4) tc::reg_fence(*reinterpret_cast<uint32_t(*)[32]>(u + 32 * c4));
+    if (!full) {
+#pragma unroll
+      for (int i = 0; i < BN; ++i)
+        if (i >= lim) u[i] = __float_as_uint(-INFINITY);
+    }
+    float mt;
+    {
       float m4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
 #pragma unroll
-      for (int c4 = 0; c4 < BN / 32; ++c4) {
-        uint32_t u[32];
-        tc::tmem_ld32(lane_base + scol + 32 * c4, u);
-        tc::tmem_wait_ld();
-#pragma unroll
-        for (int i = 0; i < 32; ++i) m4[i & 3] = fmaxf(m4[i & 3], __uint_as_float(u[i]));
-      }
+      for (int i = 0; i < BN; ++i) m4[i & 3] = fmaxf(m4[i & 3], __uint_as_float(u[i]));
       mt = fmaxf(fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3]));
-    } else {
-#pragma unroll
-      for (int c4 = 0; c4 < BN / 32; ++c4) {
-        uint32_t u[32];
-        tc::tmem_ld32(lane_base + scol + 32 * c4, u);
-        tc::tmem_wait_ld();
-#pragma unroll
-        for (int i = 0; i < 32; ++i)
-          if (32 * c4 + i < lim) mt = fmaxf(mt, __uint_as_float(u[i]));
-      }
     }
     // The reference max of a row moves only when the row's max grows by more
     // than 2^8 (then O and l are rescaled, factor 1 for rows that keep theirs;
-    // tcgen05.ld/st are warp-collective).
+    // tcgen05.ld/st are warp-collective).  O is rescaled after the P stores,
+    // once the score registers are free, and before P V is released.
     const bool need = mt > m_ref + 8.f;
     const float factor = need ? fast_exp2(m_ref - mt) : 1.f;  // 0 on a row's first visible tile
-    if (__any_sync(0xffffffffu, need) && j >= 1) {
-      // the chain's previous P V must have finished
-      if (!warp_wait_t<true>(&o_ready[grp], (j - 1) & 1, abort_s)) { ok = false; break; }
-      tc::fence_after_sync();
-#pragma unroll
-      for (int c4 = 0; c4 < D / 32; ++c4) {
-        uint32_t u[32];
-        tc::tmem_ld32(lane_base + ocol + 32 * c4, u);
-        tc::tmem_wait_ld();
-#pragma unroll
-        for (int i = 0; i < 32; ++i) u[i] = __float_as_uint(__uint_as_float(u[i]) * factor);
-        tc::tmem_st32(lane_base + ocol + 32 * c4, u);
-      }
-      tc::tmem_wait_st();
-    }
+    const bool rescale = __any_sync(0xffffffffu, need) && j >= 1;
     if (need) {
       l *= factor;
       m_ref = mt;
     }
-    // pass 2: P = exp2(s - m_ref) into the S columns, 32 keys at a time (S
-    // re-read from TMEM): keys 32c .. 32c + 31 go to columns [32c, 32c + 16)
-    // as 16-bit pairs, their lo parts to [32c + 16, 32c + 32); every store
-    // lands on columns this pass has already read.  Masked keys get s = -inf.
-    // (a row with no visible key so far has m_ref = -inf and only masked keys here)
+    // P = exp2(s - m_ref) into the S columns, 32 keys at a time: keys
+    // 32c .. 32c + 31 go to columns [32c, 32c + 16) as 16-bit pairs, their lo
+    // parts to [32c + 16, 32c + 32).  (A row with no visible key so far has
+    // m_ref = -inf and only masked keys here.)
     const float mneg = m_ref == -INFINITY ? 0.f : -m_ref;
     const float2 negm = make_float2(mneg, mneg);
     float2 ls = make_float2(0.f, 0.f);
 #pragma unroll
     for (int c = 0; c < BN / 32; ++c) {
-      uint32_t u[32];
-      tc::tmem_ld32(lane_base + scol + 32 * c, u);
-      tc::tmem_wait_ld();
-      if (!full) {
-#pragma unroll
-        for (int i = 0; i < 32; ++i)
-          if (32 * c + i >= lim) u[i] = __float_as_uint(-INFINITY);
-      }
       uint32_t uh[16], ul[16];
 #pragma unroll
       for (int i = 0; i < 16; ++i) {
-        const float2 x = add2(make_float2(__uint_as_float(u[2 * i]), __uint_as_float(u[2 * i + 1])), negm);
+        const float2 x = add2(make_float2(__uint_as_float(u[32 * c + 2 * i]), __uint_as_float(u[32 * c + 2 * i + 1])), negm);
         const float2 e = make_float2(fast_exp2(x.x), fast_exp2(x.y));
         ls = add2(ls, e);
         p_pair(e.x, e.y, uh[i], ul[i], (T*)nullptr);
@@ -550,9 +523,25 @@ __device__ __forceinline__ void softmax_chain(const Params& p, unsigned char* sm
       if constexpr (C::SPLIT) tc::tmem_st16(lane_base + scol + 32 * c + 16, ul);
     }
     l += ls.x + ls.y;
+    if (rescale) {
+      // the chain's previous P V must have finished
+      if (!warp_wait_t<true>(&o_ready[grp], (j - 1) & 1, abort_s)) { ok = false; break; }
+      tc::fence_after_sync();
+#pragma unroll
+      for (int c4 = 0; c4 < D / 32; ++c4) {
+        uint32_t o[32];
+        tc::tmem_ld32(lane_base + ocol + 32 * c4, o);
+        tc::tmem_wait_ld();
+#pragma unroll
+        for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * factor);
+        tc::tmem_st32(lane_base + ocol + 32 * c4, o);
+      }
+    }
+    // every lane's P (and O) stores complete, then one arrival per warp
     tc::tmem_wait_st();
     tc::fence_before_sync();
-    arrive_to_leader<true>(&p_full[grp]);
+    __syncwarp();
+    if (lane == 0) arrive_to_leader<true>(&p_full[grp]);
   }
 
   // epilogue: O / l -> out, 32 columns at a time
