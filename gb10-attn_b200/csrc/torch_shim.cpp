@@ -16,7 +16,8 @@
 //
 // plus the pool writer and helpers the reference keeps in Python
 // (write_kv, validate_block_tables, paged_attention_v3_lse, merge_states), and
-// the FP8-pool additions (paged_attention_v3_fp8, write_kv_scaled).
+// the FP8-pool additions (paged_attention_v3_fp8, write_kv_scaled) and the
+// many-sequence writer (write_kv_batch).
 //
 // Differences, all supersets: bf16 pools are accepted (the reference's
 // AT_DISPATCH_FLOATING_TYPES_AND_HALF has fp32/fp64/fp16 only); launches go to
@@ -367,6 +368,73 @@ void write_kv_scaled(std::vector<torch::Tensor> k_layers, std::vector<torch::Ten
                 v_scales, "write_kv_scaled");
 }
 
+// Many sequences in one call (pa_write_kv_batch): entry i of block_ids,
+// starts, ks, vs is one write_kv call's (block_ids, start, k, v).  All sources
+// are converted to one dtype (fp32 when they differ).
+void write_kv_batch(std::vector<torch::Tensor> k_layers, std::vector<torch::Tensor> v_layers,
+                    std::vector<torch::Tensor> block_ids, std::vector<int64_t> starts,
+                    std::vector<torch::Tensor> ks, std::vector<torch::Tensor> vs,
+                    torch::Tensor k_scales, torch::Tensor v_scales) {
+  const char* op = "write_kv_batch";
+  TORCH_CHECK(!k_layers.empty() && k_layers.size() == v_layers.size(),
+              op, ": need one K and one V tensor per layer");
+  const size_t n = block_ids.size();
+  TORCH_CHECK(starts.size() == n && ks.size() == n && vs.size() == n,
+              op, ": block_ids, starts, ks and vs need one entry per sequence");
+  const torch::Tensor& k0 = k_layers[0];
+  TORCH_CHECK(k0.is_cuda() && k0.dim() == 4, op, ": pool tensors must be CUDA [NB, BS, H, D]");
+  const c10::cuda::CUDAGuard guard(k0.device());
+  const int64_t L = (int64_t)k_layers.size();
+  std::vector<void*> kp, vp;
+  const int pdt = pool_dtype(k0, op);
+  for (int64_t l = 0; l < L; ++l) {
+    for (const torch::Tensor* t : {&k_layers[l], &v_layers[l]}) {
+      TORCH_CHECK(t->is_contiguous() && t->sizes() == k0.sizes() &&
+                      t->scalar_type() == k0.scalar_type() && t->device() == k0.device(),
+                  op, ": pool tensors must be contiguous and alike");
+    }
+    kp.push_back(k_layers[l].data_ptr());
+    vp.push_back(v_layers[l].data_ptr());
+  }
+  // one source dtype for the call
+  torch::ScalarType sty = n ? ks[0].scalar_type() : torch::kFloat;
+  for (size_t i = 0; i < n; ++i)
+    if (ks[i].scalar_type() != sty || vs[i].scalar_type() != sty) sty = torch::kFloat;
+  if (sty != torch::kFloat && sty != torch::kHalf && sty != torch::kBFloat16) sty = torch::kFloat;
+  const int sdt = sty == torch::kHalf ? PA_DTYPE_F16 : sty == torch::kBFloat16 ? PA_DTYPE_BF16
+                                                                                : PA_DTYPE_F32;
+  std::vector<torch::Tensor> keep;  // device copies alive until the launch is queued
+  std::vector<pa_kv_seq> seqs(n);
+  for (size_t i = 0; i < n; ++i) {
+    TORCH_CHECK(ks[i].dim() == 4 && vs[i].sizes() == ks[i].sizes() && ks[i].size(0) == L &&
+                    ks[i].size(1) == k0.size(2) && ks[i].size(3) == k0.size(3),
+                op, ": k, v of each sequence must be [n_layer, HKV, T, D] matching the pool");
+    torch::Tensor kd = ks[i].to(k0.device(), sty);
+    torch::Tensor vd = vs[i].to(k0.device(), sty);
+    if (kd.stride(3) != 1 || vd.stride(3) != 1 || vd.strides() != kd.strides()) {
+      kd = kd.contiguous();
+      vd = vd.contiguous();
+    }
+    torch::Tensor ids = block_ids[i].to(k0.device(), torch::kInt32).contiguous();
+    seqs[i] = pa_kv_seq{kd.data_ptr(), vd.data_ptr(), kd.stride(0), kd.stride(1), kd.stride(2),
+                        ids.data_ptr<int32_t>(), ids.numel(), starts[i], kd.size(2)};
+    keep.push_back(kd);
+    keep.push_back(vd);
+    keep.push_back(ids);
+  }
+  torch::Tensor ksc, vsc;
+  if (k_scales.defined() && k_scales.numel()) ksc = k_scales.to(k0.device(), torch::kFloat).contiguous();
+  if (v_scales.defined() && v_scales.numel()) vsc = v_scales.to(k0.device(), torch::kFloat).contiguous();
+  for (const torch::Tensor* t : {&ksc, &vsc})
+    TORCH_CHECK(!t->defined() || t->numel() == L * k0.size(2), op, ": scales must be [n_layer, HKV]");
+  check_status(pa_write_kv_batch(kp.data(), vp.data(), pdt, sdt, seqs.data(), (int64_t)n, L,
+                                 k0.size(2), k0.size(3), k0.size(1), k0.size(0),
+                                 ksc.defined() ? ksc.data_ptr<float>() : nullptr,
+                                 vsc.defined() ? vsc.data_ptr<float>() : nullptr, nullptr,
+                                 stream_ptr()),
+               op);
+}
+
 // One decode step's append: k_new / v_new [n_layer, B, HKV, D] go to position
 // positions[b] (< 0: skipped) of sequence b through its block-table row.
 // k_scales / v_scales: FP8 pools only ([n_layer, HKV], may be empty tensors).
@@ -472,6 +540,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("paged_attention_prefill_simt", &paged_attention_prefill_simt);
   m.def("write_kv", &write_kv);
   m.def("write_kv_scaled", &write_kv_scaled);
+  m.def("write_kv_batch", &write_kv_batch);
   m.def("append_kv", &append_kv);
   m.def("paged_attention_v3_fp8", &paged_attention_v3_fp8);
   m.def("validate_block_tables", &validate_block_tables);

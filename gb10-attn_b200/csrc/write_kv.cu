@@ -1,5 +1,6 @@
-// write_kv.cu -- KV-pool writer (C ABI pa_write_kv, pa_write_kv_scaled) and the
-// batched one-token append of a decode step (pa_append_kv).
+// write_kv.cu -- KV-pool writer (C ABI pa_write_kv, pa_write_kv_scaled), its
+// many-sequence form (pa_write_kv_batch) and the batched one-token append of
+// a decode step (pa_append_kv).
 //
 // Replaces hetero-serve TorchBlockAllocator.write_kv(block_ids, start, k, v)
 // (heteroserve/kv/torch_blocks.py:92, un-vendored; behaviour from the call
@@ -177,6 +178,131 @@ __global__ void __launch_bounds__(256) write_kv_kernel(const __grid_constant__ P
   }
 }
 
+// Batched writer (pa_write_kv_batch): up to kMaxSeqs sequences per launch,
+// each with its own source, strides, block ids, start and token count.  Work
+// rows are numbered sequence by sequence (row0[s] .. row0[s + 1]); within a
+// sequence, as in write_kv_kernel, row = (2 l + kv) T + t.
+constexpr int kMaxSeqs = 32;
+
+struct SeqDesc {
+  const char* k_src;  // this launch's first layer
+  const char* v_src;
+  int64_t layer_stride, head_stride, token_stride;  // elements
+  const int32_t* block_ids;
+  int64_t n_ids, start, T;
+};
+
+struct BatchParams {
+  char* k_layers[kMaxLayers];
+  char* v_layers[kMaxLayers];
+  SeqDesc seq[kMaxSeqs];
+  int64_t row0[kMaxSeqs + 1];
+  int32_t n_seqs;
+  int64_t L, HKV, D, BS, NB;
+  const float* k_scales;  // FP8 pools: [L, HKV] of this launch's layers (null = 1)
+  const float* v_scales;
+  int32_t* dev_status;
+};
+
+template <typename S, typename P, bool VEC>
+__global__ void __launch_bounds__(256) write_kv_batch_kernel(const __grid_constant__ BatchParams p,
+                                                             int32_t per_tok, int32_t per_head_shift,
+                                                             int32_t rpi) {
+  constexpr int E = VEC ? 8 : 1;
+  const int32_t per_head = (int32_t)(p.D / E);
+  const int64_t n_rows = p.row0[p.n_seqs];
+  const int sub = threadIdx.x / per_tok;
+  const int32_t c0 = threadIdx.x - sub * per_tok;
+  const int32_t cstep = rpi > 1 ? per_tok : (int32_t)blockDim.x;
+  if (sub >= rpi) return;
+  int s = 0;  // rows only grow along the loop, so the sequence index does too
+  for (int64_t row = (int64_t)blockIdx.x * rpi + sub; row < n_rows;
+       row += (int64_t)gridDim.x * rpi) {
+    while (s + 1 < p.n_seqs && p.row0[s + 1] <= row) ++s;
+    const SeqDesc& q = p.seq[s];
+    const int64_t r = row - p.row0[s];
+    const int64_t t = r % q.T;
+    const int64_t lk = r / q.T;
+    const int kv = (int)(lk & 1);
+    const int64_t l = lk >> 1;
+    const int64_t pos = q.start + t;
+    const int64_t page = pos / p.BS;
+    if (page >= q.n_ids) {
+      if (c0 == 0) report(p.dev_status, PA_DEVERR_BLOCK_ID);
+      continue;
+    }
+    const int64_t blk = q.block_ids[page];
+    if (blk < 0 || blk >= p.NB) {
+      if (c0 == 0) report(p.dev_status, PA_DEVERR_BLOCK_ID);
+      continue;
+    }
+    const S* src = reinterpret_cast<const S*>(kv ? q.v_src : q.k_src) + l * q.layer_stride +
+                   t * q.token_stride;
+    P* dst = reinterpret_cast<P*>(kv ? p.v_layers[l] : p.k_layers[l]) +
+             (blk * p.BS + (pos - page * p.BS)) * p.HKV * p.D;
+    const float* sc = kv ? p.v_scales : p.k_scales;
+    for (int32_t c = c0; c < per_tok; c += cstep) {
+      const int32_t h = per_head_shift >= 0 ? (c >> per_head_shift) : c / per_head;
+      const int32_t ch = c - h * per_head;
+      float qs = 1.f;  // FP8: stored value = x / scale
+      if constexpr (sizeof(P) == 1) {
+        if (sc) qs = sc[l * p.HKV + h];
+      }
+      convert_chunk<S, P, VEC>(src + h * q.head_stride + (int64_t)ch * E, dst + (int64_t)c * E, qs);
+    }
+  }
+}
+
+// Launch geometry shared by both writers: element groups per token row, rows
+// per CTA iteration, the head shift and the grid (SMs x 16 at most).
+struct Geometry {
+  int64_t per_tok;
+  int rpi, shift;
+  int64_t blocks;
+};
+static int geometry(int64_t D, int64_t HKV, int64_t n_rows, bool vec, Geometry* g) {
+  const int64_t per_head = vec ? D / 8 : D;
+  g->per_tok = HKV * per_head;
+  if (g->per_tok > (int64_t(1) << 30)) return PA_ERR_TOO_LARGE;
+  int sms = 148;
+  if (device_sm_count(&sms) != PA_OK) return PA_ERR_NO_DEVICE;
+  constexpr int kThreads = 256;
+  g->rpi = g->per_tok >= kThreads ? 1 : (int)(kThreads / g->per_tok);
+  g->shift = -1;
+  if ((per_head & (per_head - 1)) == 0) {
+    g->shift = 0;
+    while ((int64_t(1) << g->shift) < per_head) ++g->shift;
+  }
+  g->blocks = std::max<int64_t>(1, std::min<int64_t>((n_rows + g->rpi - 1) / g->rpi, (int64_t)sms * 16));
+  return PA_OK;
+}
+
+template <typename S, typename P>
+static int launch_batch_typed(const BatchParams& p, bool vec, cudaStream_t s) {
+  const int64_t n_rows = p.row0[p.n_seqs];
+  if (n_rows == 0) return PA_OK;
+  Geometry g;
+  const int st = geometry(p.D, p.HKV, n_rows, vec, &g);
+  if (st != PA_OK) return st;
+  if (vec)
+    write_kv_batch_kernel<S, P, true><<<(unsigned)g.blocks, 256, 0, s>>>(p, (int32_t)g.per_tok, g.shift, g.rpi);
+  else
+    write_kv_batch_kernel<S, P, false><<<(unsigned)g.blocks, 256, 0, s>>>(p, (int32_t)g.per_tok, g.shift, g.rpi);
+  return cuda_status(cudaGetLastError());
+}
+
+template <typename S>
+static int launch_batch_src(const BatchParams& p, int pool_dtype, bool vec, cudaStream_t s) {
+  switch (pool_dtype) {
+    case PA_DTYPE_F16: return launch_batch_typed<S, __half>(p, vec, s);
+    case PA_DTYPE_BF16: return launch_batch_typed<S, __nv_bfloat16>(p, vec, s);
+    case PA_DTYPE_F32: return launch_batch_typed<S, float>(p, vec, s);
+    case PA_DTYPE_F64: return launch_batch_typed<S, double>(p, vec, s);
+    case PA_DTYPE_E4M3: return launch_batch_typed<S, __nv_fp8_e4m3>(p, vec, s);
+    default: return PA_ERR_DTYPE;
+  }
+}
+
 template <typename S, typename P>
 static int launch_typed(const Params& p, bool vec, cudaStream_t s) {
   const int64_t per_head = vec ? p.D / 8 : p.D;
@@ -289,6 +415,91 @@ extern "C" int pa_write_kv_scaled(void* const* k_layers, void* const* v_layers, 
       default: st = writekv::launch_src<__nv_bfloat16>(p, pool_dtype, vec, s); break;
     }
     if (st) return st;
+  }
+  return PA_OK;
+}
+
+extern "C" int pa_write_kv_batch(void* const* k_layers, void* const* v_layers, int pool_dtype,
+                                 int src_dtype, const pa_kv_seq* seqs, int64_t num_seqs,
+                                 int64_t num_layers, int64_t num_kv_heads, int64_t head_dim,
+                                 int64_t block_size, int64_t num_blocks, const float* k_scales,
+                                 const float* v_scales, int32_t* dev_status, void* stream) {
+  using namespace pa;
+  using writekv::kMaxLayers;
+  using writekv::kMaxSeqs;
+  if (num_seqs < 0 || num_layers < 0 || num_kv_heads <= 0 || head_dim <= 0 || block_size <= 0 ||
+      num_blocks < 0)
+    return PA_ERR_INVALID_ARGUMENT;
+  if (num_seqs == 0 || num_layers == 0) return PA_OK;
+  if (!k_layers || !v_layers || !seqs) return PA_ERR_INVALID_ARGUMENT;
+  if (src_dtype != PA_DTYPE_F32 && src_dtype != PA_DTYPE_F16 && src_dtype != PA_DTYPE_BF16)
+    return PA_ERR_DTYPE;
+  const int ps = dtype_size(pool_dtype), ss = dtype_size(src_dtype);
+  if (ps == 0) return PA_ERR_DTYPE;
+  // every sequence is checked before anything is launched
+  bool vec_src = head_dim % 8 == 0 && (head_dim * ps) % 16 == 0;
+  for (int64_t i = 0; i < num_seqs; ++i) {
+    const pa_kv_seq& q = seqs[i];
+    if (q.num_tokens < 0 || q.start < 0 || q.num_block_ids < 0) return PA_ERR_INVALID_ARGUMENT;
+    if (q.num_tokens == 0) continue;
+    if (!q.k_src || !q.v_src || !q.block_ids) return PA_ERR_INVALID_ARGUMENT;
+    vec_src = vec_src && aligned16(q.k_src) && aligned16(q.v_src) &&
+              (q.src_layer_stride * ss) % 16 == 0 && (q.src_head_stride * ss) % 16 == 0 &&
+              (q.src_token_stride * ss) % 16 == 0;
+  }
+  for (int64_t l = 0; l < num_layers; ++l) {
+    if (!k_layers[l] || !v_layers[l]) return PA_ERR_INVALID_ARGUMENT;
+    vec_src = vec_src && aligned16(k_layers[l]) && aligned16(v_layers[l]);
+  }
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  for (int64_t l0 = 0; l0 < num_layers; l0 += kMaxLayers) {
+    const int64_t nl = std::min<int64_t>(kMaxLayers, num_layers - l0);
+    int64_t i = 0;
+    while (i < num_seqs) {
+      writekv::BatchParams p = {};
+      for (int64_t l = 0; l < nl; ++l) {
+        p.k_layers[l] = static_cast<char*>(k_layers[l0 + l]);
+        p.v_layers[l] = static_cast<char*>(v_layers[l0 + l]);
+      }
+      // the next (up to) kMaxSeqs sequences with tokens
+      int n = 0;
+      int64_t rows = 0;
+      for (; i < num_seqs && n < kMaxSeqs; ++i) {
+        const pa_kv_seq& q = seqs[i];
+        if (q.num_tokens == 0) continue;
+        writekv::SeqDesc& d = p.seq[n];
+        d.k_src = static_cast<const char*>(q.k_src) + l0 * q.src_layer_stride * ss;
+        d.v_src = static_cast<const char*>(q.v_src) + l0 * q.src_layer_stride * ss;
+        d.layer_stride = q.src_layer_stride;
+        d.head_stride = q.src_head_stride;
+        d.token_stride = q.src_token_stride;
+        d.block_ids = q.block_ids;
+        d.n_ids = q.num_block_ids;
+        d.start = q.start;
+        d.T = q.num_tokens;
+        p.row0[n] = rows;
+        rows += nl * 2 * q.num_tokens;
+        ++n;
+      }
+      if (n == 0) break;
+      p.row0[n] = rows;
+      p.n_seqs = n;
+      p.L = nl;
+      p.HKV = num_kv_heads;
+      p.D = head_dim;
+      p.BS = block_size;
+      p.NB = num_blocks;
+      p.k_scales = k_scales ? k_scales + l0 * num_kv_heads : nullptr;
+      p.v_scales = v_scales ? v_scales + l0 * num_kv_heads : nullptr;
+      p.dev_status = dev_status;
+      int st;
+      switch (src_dtype) {
+        case PA_DTYPE_F32: st = writekv::launch_batch_src<float>(p, pool_dtype, vec_src, s); break;
+        case PA_DTYPE_F16: st = writekv::launch_batch_src<__half>(p, pool_dtype, vec_src, s); break;
+        default: st = writekv::launch_batch_src<__nv_bfloat16>(p, pool_dtype, vec_src, s); break;
+      }
+      if (st) return st;
+    }
   }
   return PA_OK;
 }

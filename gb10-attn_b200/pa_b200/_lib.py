@@ -36,6 +36,15 @@ _I64 = ctypes.c_int64
 _D = ctypes.c_double
 _SZ = ctypes.c_size_t
 
+
+
+class PaKvSeq(ctypes.Structure):
+    """``pa_kv_seq`` of include/pa_b200.h: one sequence of pa_write_kv_batch."""
+    _fields_ = [("k_src", _P), ("v_src", _P), ("src_layer_stride", _I64),
+                ("src_head_stride", _I64), ("src_token_stride", _I64), ("block_ids", _P),
+                ("num_block_ids", _I64), ("start", _I64), ("num_tokens", _I64)]
+
+
 # name -> (restype, argtypes); mirrors include/pa_b200.h
 _DECODE = [_P, _P, _I, _P, _P] + [_I64] * 7 + [_D]
 SIGNATURES = {
@@ -76,6 +85,7 @@ SIGNATURES = {
                     [_P, _P]),
     "pa_write_kv_scaled": (_I, [_P, _P, _I, _P, _P, _I, _I64, _I64, _I64, _P] + [_I64] * 8 +
                            [_P, _P, _P, _P]),
+    "pa_write_kv_batch": (_I, [_P, _P, _I, _I, _P, _I64] + [_I64] * 5 + [_P, _P, _P, _P]),
     "pa_append_kv": (_I, [_P, _P, _I, _P, _P, _I, _P, _I64, _P] + [_I64] * 6 +
                      [_P, _P, _P, _P]),
     "pa_validate_block_tables": (_I, [_P, _P, _I64, _I64, _I64, _I64, _P, _P]),

@@ -250,6 +250,28 @@ class TorchBlockAllocator:
         cache[key] = ids  # most recently used last
         return ids
 
+    def write_kv_batch(self, block_id_lists, starts, ks, vs) -> None:
+        """write_kv for several sequences in one call (one kernel launch for up
+        to 32 sequences): entry i of each argument is one write_kv call's
+        (block_ids, start, k, v).  Sequences must not share pool rows."""
+        from . import ops
+
+        def dev(x):
+            t = torch.from_numpy(np.ascontiguousarray(x)) if isinstance(x, np.ndarray) else x
+            if t.device.type == "cpu":
+                t = t.pin_memory().to(self.device, non_blocking=True)
+            return t
+
+        ids = [b.to(device=self.device, dtype=torch.int32) if isinstance(b, torch.Tensor)
+               else self._device_ids(b) for b in block_id_lists]
+        n_layer = self.model_cfg.n_layer
+        kl = [self.pool[layer, 0] for layer in range(n_layer)]
+        vl = [self.pool[layer, 1] for layer in range(n_layer)]
+        empty = torch.empty(0)
+        ops.write_kv_batch(kl, vl, ids, [int(s) for s in starts], [dev(k) for k in ks],
+                           [dev(v) for v in vs], self.k_scales if self.fp8 else empty,
+                           self.v_scales if self.fp8 else empty)
+
     def write_kv(self, block_ids, start: int, k, v) -> None:
         """Write K/V of one sequence for every layer.
 

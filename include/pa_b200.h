@@ -367,6 +367,33 @@ PA_API int pa_write_kv_scaled(void* const* k_layers, void* const* v_layers, int 
                               const float* k_scales, const float* v_scales,
                               int32_t* dev_status, void* stream);
 
+/* One sequence of a pa_write_kv_batch call: the arguments pa_write_kv takes
+ * per sequence.  k_src / v_src: device [num_layers, num_kv_heads, num_tokens,
+ * head_dim] of the call's src_dtype, head_dim contiguous, the given element
+ * strides; block_ids: device int32 [num_block_ids]; token t lands at sequence
+ * position start + t. */
+typedef struct pa_kv_seq {
+  const void* k_src;
+  const void* v_src;
+  int64_t src_layer_stride, src_head_stride, src_token_stride;
+  const int32_t* block_ids;
+  int64_t num_block_ids;
+  int64_t start;
+  int64_t num_tokens;
+} pa_kv_seq;
+
+/* pa_write_kv_scaled for many sequences in one call, an addition (the
+ * reference's TorchBlockAllocator.write_kv, heteroserve/kv/torch_blocks.py:92,
+ * writes one sequence per call, as pa_write_kv does): the result equals one
+ * pa_write_kv_scaled per entry of `seqs` (a HOST array of num_seqs), with up
+ * to 32 sequences and 64 layers per kernel launch.  Entries are validated
+ * before anything is launched; sequences must not write the same pool row. */
+PA_API int pa_write_kv_batch(void* const* k_layers, void* const* v_layers, int pool_dtype,
+                             int src_dtype, const pa_kv_seq* seqs, int64_t num_seqs,
+                             int64_t num_layers, int64_t num_kv_heads, int64_t head_dim,
+                             int64_t block_size, int64_t num_blocks, const float* k_scales,
+                             const float* v_scales, int32_t* dev_status, void* stream);
+
 /* One decode step's K/V append for a batch, an addition (the reference
  * writes whole sequences with write_kv only): for every layer l < num_layers,
  * sequence b < num_seqs with positions[b] >= 0 and kv head h,

@@ -130,6 +130,36 @@ def test_write_kv_argument_checks():
     assert st == 0  # zero tokens: nothing to do
 
 
+def test_write_kv_batch_argument_checks():
+    one = (ctypes.c_void_p * 1)(16)
+    seqs = (_lib.PaKvSeq * 2)()
+    bad = _lib.PA_ERR_INVALID_ARGUMENT
+    args = (1, 2, 64, 16, 8, None, None, None, None)
+    # null sequence array with sequences to write, negative counts
+    assert _lib.call("pa_write_kv_batch", one, one, _lib.PA_DTYPE_F16, _lib.PA_DTYPE_F32,
+                     None, 2, *args) == bad
+    assert _lib.call("pa_write_kv_batch", one, one, _lib.PA_DTYPE_F16, _lib.PA_DTYPE_F32,
+                     seqs, -1, *args) == bad
+    seqs[1].num_tokens = -3
+    assert _lib.call("pa_write_kv_batch", one, one, _lib.PA_DTYPE_F16, _lib.PA_DTYPE_F32,
+                     seqs, 2, *args) == bad
+    # a sequence with tokens but no source
+    seqs[1].num_tokens = 4
+    assert _lib.call("pa_write_kv_batch", one, one, _lib.PA_DTYPE_F16, _lib.PA_DTYPE_F32,
+                     seqs, 2, *args) == bad
+    # dtypes the writer does not handle
+    assert _lib.call("pa_write_kv_batch", one, one, _lib.PA_DTYPE_F16, _lib.PA_DTYPE_E4M3,
+                     seqs, 2, *args) == _lib.PA_ERR_DTYPE
+    assert _lib.call("pa_write_kv_batch", one, one, 17, _lib.PA_DTYPE_F32,
+                     seqs, 2, *args) == _lib.PA_ERR_DTYPE
+    # nothing to write: no sequences, or only empty ones
+    assert _lib.call("pa_write_kv_batch", None, None, _lib.PA_DTYPE_F16, _lib.PA_DTYPE_F32,
+                     None, 0, *args) == 0
+    seqs[1].num_tokens = 0
+    assert _lib.call("pa_write_kv_batch", one, one, _lib.PA_DTYPE_F16, _lib.PA_DTYPE_F32,
+                     seqs, 2, *args) == 0
+
+
 def test_torch_shim_imports_on_cpu():
     from pa_b200 import ops
     assert ops.shim_path().exists()
