@@ -104,6 +104,7 @@ struct PlanParams {
   int32_t NGC, N;
   int32_t tt;  // tokens per tile
   float empty_fill;
+  int32_t io_dtype;  // element type of out
 };
 
 // One CTA: tile counts -> exclusive scan -> tile_off; the sequence holding
@@ -132,7 +133,7 @@ __global__ void __launch_bounds__(kPlanThreads) plan_kernel(const __grid_constan
       if (n > pp.max_ctx) n = pp.max_ctx;
       if (n <= 0) {
         n = 0;
-        for (int64_t i = 0; i < pp.H * pp.D; ++i) pp.out[b * pp.H * pp.D + i] = pp.empty_fill;
+        for (int64_t i = 0; i < pp.H * pp.D; ++i) io_store(pp.io_dtype, pp.out, b * pp.H * pp.D + i, pp.empty_fill);
         if (pp.lse)
           for (int64_t h = 0; h < pp.H; ++h) pp.lse[b * pp.H + h] = -INFINITY;
       }
@@ -246,6 +247,13 @@ static int check_args(const DecodeArgs& a) {
   if (a.D != 32 && a.D != 64 && a.D != 128 && a.D != 256) return PA_ERR_HEAD_DIM;
   if (dtype_size(a.dtype) == 0) return PA_ERR_DTYPE;
   if (a.qlen < 1) return PA_ERR_INVALID_ARGUMENT;
+  if (a.io_dtype != PA_DTYPE_F32 && a.io_dtype != PA_DTYPE_F16 && a.io_dtype != PA_DTYPE_BF16)
+    return PA_ERR_DTYPE;
+  // the step's append: decode only, both rows or neither, a pool it writes
+  // without scales (FP8 pools take pa_append_kv)
+  if ((a.k_new == nullptr) != (a.v_new == nullptr) || (a.k_new && a.qlen != 1))
+    return PA_ERR_INVALID_ARGUMENT;
+  if (a.k_new && a.dtype == PA_DTYPE_E4M3) return PA_ERR_DTYPE;
   if (a.B * a.qlen > (int64_t(1) << 30) || a.MB * a.BS > (int64_t(1) << 31) - 2 * kTT)
     return PA_ERR_TOO_LARGE;
   return PA_OK;
@@ -378,6 +386,7 @@ int launch(const DecodeArgs& a, void* ws, size_t ws_bytes, cudaStream_t stream) 
   pp.N = c.N;
   pp.empty_fill = a.empty_fill;
   pp.tt = c.tt;
+  pp.io_dtype = a.io_dtype;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = 1;
@@ -438,6 +447,9 @@ int launch(const DecodeArgs& a, void* ws, size_t ws_bytes, cudaStream_t stream) 
     for (int sh = 0; sh < 32; ++sh)
       if ((int64_t(1) << sh) == a.BS) p.bs_shift = sh;
   p.blk_stride = a.BS * p.tok_stride;
+  p.io_dtype = a.io_dtype;
+  p.k_new = static_cast<const char*>(a.k_new);
+  p.v_new = static_cast<const char*>(a.v_new);
 
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)c.N);
@@ -600,6 +612,46 @@ extern "C" int pa_paged_attention_v3(float* out, float* lse, const float* q, con
                       num_seqs, num_heads, num_kv_heads, head_dim, block_size, num_blocks,
                       max_blocks, scale, num_splits, workspace, workspace_bytes, dev_status,
                       stream);
+}
+
+// One layer of a decode step (an addition): q / out in io_dtype, and when
+// k_new / v_new are given, sequence b's new K / V row written at position
+// context_lens[b] - 1 of its pages inside the same launch, before the tile
+// that holds it is read.
+extern "C" int pa_decode_layer_step(void* out, float* lse, const void* q, int io_dtype,
+                                    void* k_cache, void* v_cache, int kv_dtype,
+                                    const void* k_new, const void* v_new,
+                                    const int32_t* block_tables, const int32_t* context_lens,
+                                    int64_t num_seqs, int64_t num_heads, int64_t num_kv_heads,
+                                    int64_t head_dim, int64_t block_size, int64_t num_blocks,
+                                    int64_t max_blocks, double scale, int64_t num_splits,
+                                    void* workspace, size_t workspace_bytes, int32_t* dev_status,
+                                    void* stream) {
+  DecodeArgs a;
+  a.out = static_cast<float*>(out);
+  a.lse = lse;
+  a.q = static_cast<const float*>(q);
+  a.k_cache = k_cache;
+  a.v_cache = v_cache;
+  a.dtype = kv_dtype;
+  a.block_tables = block_tables;
+  a.context_lens = context_lens;
+  a.B = num_seqs;
+  a.H = num_heads;
+  a.HKV = num_kv_heads;
+  a.D = head_dim;
+  a.BS = block_size;
+  a.NB = num_blocks;
+  a.MB = max_blocks;
+  a.scale = scale;
+  a.num_splits = num_splits;
+  a.dev_status = dev_status;
+  a.qlen = 1;
+  a.empty_fill = std::numeric_limits<float>::quiet_NaN();  // as pa_paged_attention_v3
+  a.io_dtype = io_dtype;
+  a.k_new = k_new;
+  a.v_new = v_new;
+  return pa::decode::launch(a, workspace, workspace_bytes, static_cast<cudaStream_t>(stream));
 }
 
 extern "C" int pa_paged_attention_v3_fp8(float* out, float* lse, const float* q,

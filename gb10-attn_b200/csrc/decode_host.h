@@ -27,6 +27,12 @@ struct DecodeArgs {
   float empty_fill = 0.f;  // value of rows that see no key
   const float* k_scale = nullptr;  // FP8 pools: [HKV] dequantisation scales (null = 1)
   const float* v_scale = nullptr;
+  // element type of q and out (PA_DTYPE_F32 / F16 / BF16; `q` and `out` point
+  // at that type), and the decode step's new K / V rows ([B, HKV, D] of
+  // io_dtype, null: none), written at position context_lens[b] - 1 first
+  int io_dtype = 0;
+  const void* k_new = nullptr;
+  const void* v_new = nullptr;
 };
 
 int launch(const DecodeArgs& a, void* ws, size_t ws_bytes, cudaStream_t stream);

@@ -105,7 +105,61 @@ struct Params {
   int64_t tok_stride;            // HKV * D * sizeof(T): one token row of a page
   int32_t bs_shift;              // log2(BS) when BS is a power of two, else -1
   int64_t blk_stride;            // BS * tok_stride: one page
+  // q / out element type (PA_DTYPE_F32 / F16 / BF16: `q` and `out` point at
+  // that type; partials and lse stay fp32) and the decode step's new K / V
+  // rows ([B, HKV, D] of io_dtype, null: none): the producer that loads a
+  // sequence's last tile first writes them at position context_lens[b] - 1.
+  int32_t io_dtype;
+  const char* k_new;
+  const char* v_new;
 };
+
+// q / out elements in the call's io type
+__device__ __forceinline__ float io_load(int io, const void* base, int64_t i) {
+  if (io == PA_DTYPE_BF16) return __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(base)[i]);
+  if (io == PA_DTYPE_F16) return __half2float(reinterpret_cast<const __half*>(base)[i]);
+  return reinterpret_cast<const float*>(base)[i];
+}
+__device__ __forceinline__ void io_store(int io, void* base, int64_t i, float x) {
+  if (io == PA_DTYPE_BF16)
+    reinterpret_cast<__nv_bfloat16*>(base)[i] = __float2bfloat16_rn(x);
+  else if (io == PA_DTYPE_F16)
+    reinterpret_cast<__half*>(base)[i] = __float2half_rn(x);
+  else
+    reinterpret_cast<float*>(base)[i] = x;
+}
+// two adjacent elements (i even): one 8- or 4-byte access
+__device__ __forceinline__ float2 io_load2(int io, const void* base, int64_t i) {
+  if (io == PA_DTYPE_F32) return *reinterpret_cast<const float2*>(reinterpret_cast<const float*>(base) + i);
+  const uint32_t w = *reinterpret_cast<const uint32_t*>(reinterpret_cast<const uint16_t*>(base) + i);
+  if (io == PA_DTYPE_BF16) return make_float2(__uint_as_float(w << 16), __uint_as_float(w & 0xffff0000u));
+  const __half2 h = *reinterpret_cast<const __half2*>(&w);
+  return __half22float2(h);
+}
+__device__ __forceinline__ void io_store2(int io, void* base, int64_t i, float2 x) {
+  if (io == PA_DTYPE_F32) {
+    *reinterpret_cast<float2*>(reinterpret_cast<float*>(base) + i) = x;
+  } else if (io == PA_DTYPE_BF16) {
+    const __nv_bfloat162 h = __floats2bfloat162_rn(x.x, x.y);
+    *reinterpret_cast<__nv_bfloat162*>(reinterpret_cast<__nv_bfloat16*>(base) + i) = h;
+  } else {
+    const __half2 h = __floats2half2_rn(x.x, x.y);
+    *reinterpret_cast<__half2*>(reinterpret_cast<__half*>(base) + i) = h;
+  }
+}
+// a pool element from fp32, rounded to nearest even (the writer's rule)
+template <typename T> __device__ __forceinline__ T pool_from_f32(float x);
+template <> __device__ __forceinline__ float pool_from_f32<float>(float x) { return x; }
+template <> __device__ __forceinline__ double pool_from_f32<double>(float x) { return (double)x; }
+template <> __device__ __forceinline__ __half pool_from_f32<__half>(float x) { return __float2half_rn(x); }
+template <> __device__ __forceinline__ __nv_bfloat16 pool_from_f32<__nv_bfloat16>(float x) {
+  return __float2bfloat16_rn(x);
+}
+template <> __device__ __forceinline__ __nv_fp8_e4m3 pool_from_f32<__nv_fp8_e4m3>(float x) {
+  __nv_fp8_e4m3 r;
+  r.__x = __nv_cvt_float_to_fp8(x, __NV_SATFINITE, __NV_E4M3);
+  return r;
+}
 
 struct __align__(16) StageHeader {
   int32_t b, gc, tok0, nvalid;
@@ -216,7 +270,7 @@ __device__ __forceinline__ void fused_plan(const Params& p, int32_t* tile_off_s,
       if (n <= 0) {
         n = 0;
         if (b % gridDim.x == blockIdx.x) {
-          for (int64_t i = 0; i < p.H * D; ++i) p.out[b * p.H * D + i] = p.empty_fill;
+          for (int64_t i = 0; i < p.H * D; ++i) io_store(p.io_dtype, p.out, b * p.H * D + i, p.empty_fill);
           if (p.lse)
             for (int64_t h = 0; h < p.H; ++h) p.lse[b * p.H + h] = -INFINITY;
         }
@@ -505,7 +559,8 @@ __global__ void __launch_bounds__(Limits<T, D, QC>::THREADS, 1)
       int nx_b = 0, nx_gc = 0;           // the next sequence of this CTA's range
       int32_t nx_cur = 0, nx_next = 0;   // its first block-table window
       const int64_t gbytes = (int64_t)p.G * D * (int64_t)sizeof(T);
-      const uint32_t qbytes = (uint32_t)(p.G * p.QPK * D * 4);
+      const int64_t qes = p.io_dtype == PA_DTYPE_F32 ? 4 : 2;  // bytes per q element
+      const uint32_t qbytes = (uint32_t)(p.G * p.QPK * D * qes);
 
       while (gt < hi) {
         const int64_t t_in_seq = r - s0;
@@ -564,8 +619,36 @@ __global__ void __launch_bounds__(Limits<T, D, QC>::THREADS, 1)
           h.seq_t0 = (int64_t)gc * Tpg + s0;
           h.seq_t1 = (int64_t)gc * Tpg + s1;
           if (first)
-            prefetch_l2(p.q + ((int64_t)b * p.H + (int64_t)gc * p.G * p.QPK) * D, qbytes);
+            prefetch_l2(reinterpret_cast<const char*>(p.q) +
+                            ((int64_t)b * p.H + (int64_t)gc * p.G * p.QPK) * D * qes,
+                        qbytes);
           mbar_arrive_expect_tx(&full[stage], (uint32_t)nvalid * 2u * p.row_bytes);
+        }
+        // Decode step with append: the sequence's new K / V row (this g-chunk's
+        // heads) goes to position context_lens[b] - 1, the last row of this
+        // tile, before the tile is copied; only this CTA reads that row.
+        if (p.k_new != nullptr && r + 1 == s1) {
+          const int64_t cb = p.context_lens[b];
+          if (cb > 0 && cb <= max_ctx) {
+            const int64_t pos = cb - 1;
+            const int64_t pg = page_of(pos);
+            const int idx = (int)(pg - win_base);
+            const int32_t a0 = __shfl_sync(0xffffffffu, win_cur, idx & 31);
+            const int32_t a1 = __shfl_sync(0xffffffffu, win_next, idx & 31);
+            const int64_t blk = idx < 32 ? a0 : a1;
+            if (blk >= 0 && blk < p.NB) {
+              const int64_t roff = blk * p.blk_stride + (pos - pg * p.BS) * p.tok_stride + (int64_t)gc * gbytes;
+              T* kd = reinterpret_cast<T*>(const_cast<char*>(p.k_cache) + roff);
+              T* vd = reinterpret_cast<T*>(const_cast<char*>(p.v_cache) + roff);
+              const int64_t src0 = ((int64_t)b * p.HKV + (int64_t)gc * p.G) * D;
+              for (int64_t e = lane; e < (int64_t)p.G * D; e += 32) {
+                kd[e] = pool_from_f32<T>(io_load(p.io_dtype, p.k_new, src0 + e));
+                vd[e] = pool_from_f32<T>(io_load(p.io_dtype, p.v_new, src0 + e));
+              }
+              // the generic-proxy stores before the bulk copies that read them
+              asm volatile("fence.proxy.async.global;" ::: "memory");
+            }
+          }
         }
         __syncwarp();
 #pragma unroll
@@ -604,7 +687,9 @@ __global__ void __launch_bounds__(Limits<T, D, QC>::THREADS, 1)
           nx_cur = lane < p.MB ? __ldg(nbt + lane) : 0;
           nx_next = 32 + lane < p.MB ? __ldg(nbt + 32 + lane) : 0;
           if (lane == 0)
-            prefetch_l2(p.q + ((int64_t)nx_b * p.H + (int64_t)nx_gc * p.G * p.QPK) * D, qbytes);
+            prefetch_l2(reinterpret_cast<const char*>(p.q) +
+                            ((int64_t)nx_b * p.H + (int64_t)nx_gc * p.G * p.QPK) * D * qes,
+                        qbytes);
         }
         ++gt;
         ++r;
@@ -692,7 +777,7 @@ __global__ void __launch_bounds__(Limits<T, D, QC>::THREADS, 1)
       for (int k = 0; k < PERG; ++k) {
         const int j = (32 * k) / D;
         const int e = (lane + 32 * k) - j * D;
-        p.out[((int64_t)pb * p.H + phead0 + j) * D + e] = __int_as_float(0x7fc00000);
+        io_store(p.io_dtype, p.out, ((int64_t)pb * p.H + phead0 + j) * D + e, __int_as_float(0x7fc00000));
       }
       if (p.lse && lane < QC) p.lse[(int64_t)pb * p.H + phead0 + lane] = __int_as_float(0x7fc00000);
       if (lane == 0) report(p.dev_status, PA_DEVERR_MERGE);
@@ -742,7 +827,7 @@ __global__ void __launch_bounds__(Limits<T, D, QC>::THREADS, 1)
       for (int k = 0; k < PER; ++k) {
         const int j = (32 * k) / D;
         const int e = (lane + 32 * k) - j * D;
-        p.out[((int64_t)pb * p.H + phead0 + j) * D + e] = o[k] / lg[j];
+        io_store(p.io_dtype, p.out, ((int64_t)pb * p.H + phead0 + j) * D + e, o[k] / lg[j]);
       }
       if (p.lse && lane < QC) {
 #pragma unroll
@@ -780,7 +865,7 @@ __global__ void __launch_bounds__(Limits<T, D, QC>::THREADS, 1)
       gc = h.gc;
       seg_gt0 = h.gt;
       head0 = ((int64_t)gc * p.G + g_local) * p.QPK + hq0;
-      const float* qp = p.q + ((int64_t)b * p.H + head0) * D;
+      const int64_t q0 = ((int64_t)b * p.H + head0) * D;  // element offset in q
       float qs = p.qscale;
       if constexpr (sizeof(T) == 1) {
         const int64_t kvh = (int64_t)gc * p.G + g_local;
@@ -791,10 +876,10 @@ __global__ void __launch_bounds__(Limits<T, D, QC>::THREADS, 1)
       for (int j = 0; j < QC; ++j) {
 #pragma unroll
         for (int c = 0; c < NCH; ++c) {
-          const float* src = qp + (int64_t)j * D + (c * R + li) * VEC;
+          const int64_t src = q0 + (int64_t)j * D + (c * R + li) * VEC;
 #pragma unroll
           for (int v = 0; v < VEC; v += 2) {
-            const float2 x = *reinterpret_cast<const float2*>(src + v);
+            const float2 x = io_load2(p.io_dtype, p.q, src + v);
             qf[j][c * VEC + v] = x.x * qs;
             qf[j][c * VEC + v + 1] = x.y * qs;
           }
@@ -938,7 +1023,7 @@ __global__ void __launch_bounds__(Limits<T, D, QC>::THREADS, 1)
 #pragma unroll
         for (int j = 0; j < QC; ++j) {
           const float inv = 1.f / l[j];
-          float* o = p.out + ((int64_t)b * p.H + head0 + j) * D;
+          const int64_t o = ((int64_t)b * p.H + head0 + j) * D;  // element offset in out
 #pragma unroll
           for (int c = 0; c < NCH; ++c) {
 #pragma unroll
@@ -946,7 +1031,7 @@ __global__ void __launch_bounds__(Limits<T, D, QC>::THREADS, 1)
               float2 y;
               y.x = acc[j][c * VEC + v] * inv;
               y.y = acc[j][c * VEC + v + 1] * inv;
-              *reinterpret_cast<float2*>(o + (c * R + li) * VEC + v) = y;
+              io_store2(p.io_dtype, p.out, o + (c * R + li) * VEC + v, y);
             }
           }
           if (p.lse && li == 0) p.lse[(int64_t)b * p.H + head0 + j] = (m[j] + __log2f(l[j])) * kLn2;

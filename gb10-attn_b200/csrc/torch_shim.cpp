@@ -17,7 +17,8 @@
 // plus the pool writer and helpers the reference keeps in Python
 // (write_kv, validate_block_tables, paged_attention_v3_lse, merge_states), and
 // the FP8-pool additions (paged_attention_v3_fp8, write_kv_scaled) and the
-// many-sequence writer (write_kv_batch).
+// many-sequence writer (write_kv_batch) and one layer of a decode step
+// (decode_layer_step: q / out in bf16 or fp16, the K/V append fused in).
 //
 // Differences, all supersets: bf16 pools are accepted (the reference's
 // AT_DISPATCH_FLOATING_TYPES_AND_HALF has fp32/fp64/fp16 only); launches go to
@@ -368,6 +369,60 @@ void write_kv_scaled(std::vector<torch::Tensor> k_layers, std::vector<torch::Ten
                 v_scales, "write_kv_scaled");
 }
 
+// One layer of a decode step (pa_decode_layer_step): q [B, H, D] of fp32 /
+// fp16 / bf16 gives out of the same dtype; k_new / v_new ([B, HKV, D], or
+// empty tensors for none) are written at position context_lens[b] - 1 of the
+// pool in the same launch.  The pool tensors are written in place.
+torch::Tensor decode_layer_step(torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_cache,
+                                torch::Tensor block_tables, torch::Tensor context_lens,
+                                double scale, torch::Tensor k_new, torch::Tensor v_new) {
+  const char* op = "decode_layer_step";
+  TORCH_CHECK(q.is_cuda() && q.dim() == 3, op, ": q must be a CUDA [B, H, D] tensor");
+  int io;
+  switch (q.scalar_type()) {
+    case torch::kFloat: io = PA_DTYPE_F32; break;
+    case torch::kHalf: io = PA_DTYPE_F16; break;
+    case torch::kBFloat16: io = PA_DTYPE_BF16; break;
+    default: TORCH_CHECK(false, op, ": q must be float32, float16 or bfloat16");
+  }
+  TORCH_CHECK(k_cache.is_cuda() && k_cache.dim() == 4 && v_cache.sizes() == k_cache.sizes() &&
+                  v_cache.scalar_type() == k_cache.scalar_type(),
+              op, ": k_cache, v_cache must be alike CUDA [NB, BS, HKV, D] tensors");
+  TORCH_CHECK(k_cache.is_contiguous() && v_cache.is_contiguous(),
+              op, ": the pool is written in place, so it must be contiguous");
+  const c10::cuda::CUDAGuard guard(q.device());
+  torch::Tensor qc = q.contiguous();
+  torch::Tensor bt = block_tables.to(q.device(), torch::kInt32).contiguous();
+  torch::Tensor ctx = context_lens.to(q.device(), torch::kInt32).contiguous();
+  const int64_t B = qc.size(0), H = qc.size(1), D = qc.size(2);
+  const int64_t NB = k_cache.size(0), BS = k_cache.size(1), HKV = k_cache.size(2);
+  TORCH_CHECK(k_cache.size(3) == D, op, ": k_cache head_dim must match q");
+  TORCH_CHECK(bt.dim() == 2 && bt.size(0) >= B && ctx.numel() >= B,
+              op, ": block_tables [B, MB] and context_lens [B] needed");
+  const int kdt = pool_dtype(k_cache, op);
+  torch::Tensor kn, vn;
+  const bool append = k_new.defined() && k_new.numel() > 0;
+  if (append) {
+    TORCH_CHECK(v_new.sizes() == k_new.sizes() && k_new.dim() == 3 && k_new.size(0) == B &&
+                    k_new.size(1) == HKV && k_new.size(2) == D,
+                op, ": k_new, v_new must be [B, HKV, D]");
+    kn = k_new.to(q.device(), q.scalar_type()).contiguous();
+    vn = v_new.to(q.device(), q.scalar_type()).contiguous();
+  }
+  torch::Tensor out = torch::empty({B, H, D}, qc.options());
+  if (B == 0) return out;
+  size_t ws_bytes = 0;
+  check_status(pa_decode_workspace_size(B, H, HKV, D, kdt, BS, bt.size(1), 0, &ws_bytes), op);
+  torch::Tensor ws = workspace(ws_bytes, qc);
+  check_status(pa_decode_layer_step(out.data_ptr(), nullptr, qc.data_ptr(), io, k_cache.data_ptr(),
+                                    v_cache.data_ptr(), kdt, append ? kn.data_ptr() : nullptr,
+                                    append ? vn.data_ptr() : nullptr, bt.data_ptr<int32_t>(),
+                                    ctx.data_ptr<int32_t>(), B, H, HKV, D, BS, NB, bt.size(1),
+                                    scale, 0, ws.data_ptr(), ws_bytes, nullptr, stream_ptr()),
+               op);
+  return out;
+}
+
 // Many sequences in one call (pa_write_kv_batch): entry i of block_ids,
 // starts, ks, vs is one write_kv call's (block_ids, start, k, v).  All sources
 // are converted to one dtype (fp32 when they differ).
@@ -541,6 +596,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("write_kv", &write_kv);
   m.def("write_kv_scaled", &write_kv_scaled);
   m.def("write_kv_batch", &write_kv_batch);
+  m.def("decode_layer_step", &decode_layer_step);
   m.def("append_kv", &append_kv);
   m.def("paged_attention_v3_fp8", &paged_attention_v3_fp8);
   m.def("validate_block_tables", &validate_block_tables);

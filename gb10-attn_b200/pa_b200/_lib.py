@@ -88,6 +88,8 @@ SIGNATURES = {
     "pa_write_kv_batch": (_I, [_P, _P, _I, _I, _P, _I64] + [_I64] * 5 + [_P, _P, _P, _P]),
     "pa_append_kv": (_I, [_P, _P, _I, _P, _P, _I, _P, _I64, _P] + [_I64] * 6 +
                      [_P, _P, _P, _P]),
+    "pa_decode_layer_step": (_I, [_P, _P, _P, _I, _P, _P, _I, _P, _P, _P, _P] + [_I64] * 7 +
+                             [_D, _I64, _P, _SZ, _P, _P]),
     "pa_validate_block_tables": (_I, [_P, _P, _I64, _I64, _I64, _I64, _P, _P]),
 }
 

@@ -231,6 +231,31 @@ class TorchBlockAllocator:
                       self.k_scales if self.fp8 else empty,
                       self.v_scales if self.fp8 else empty)
 
+    def decode_step(self, q_layers, block_tables, context_lens, k_new=None, v_new=None,
+                    scale: float | None = None):
+        """One decode step of the engine: for every layer, the sequences' new
+        K / V row appended at position context_lens[b] - 1 and the attention
+        over the grown context, in one launch per layer (pa_decode_layer_step).
+
+        q_layers: [n_layer, B, n_head, head_dim] (fp32 / fp16 / bf16; the
+        outputs have the same dtype); k_new, v_new: [n_layer, B, n_kv_head,
+        head_dim] or None (nothing appended); context_lens counts the new
+        token.  Returns [n_layer, B, n_head, head_dim]."""
+        from . import ops
+        n_layer = self.model_cfg.n_layer
+        d = q_layers.shape[-1]
+        sc = d ** -0.5 if scale is None else float(scale)
+        bt = torch.as_tensor(block_tables).to(self.device, torch.int32)
+        ctx = torch.as_tensor(context_lens).to(self.device, torch.int32)
+        empty = torch.empty(0, device=self.device)
+        outs = []
+        for layer in range(n_layer):
+            kc, vc = self.pool[layer, 0], self.pool[layer, 1]
+            kn = empty if k_new is None else k_new[layer]
+            vn = empty if v_new is None else v_new[layer]
+            outs.append(ops.decode_layer_step(q_layers[layer], kc, vc, bt, ctx, sc, kn, vn))
+        return torch.stack(outs)
+
     # -- writer ----------------------------------------------------------------
     _IDS_CACHE_MAX = 4096
 

@@ -47,12 +47,13 @@ paged_attention_v3_fp8 = _ext.paged_attention_v3_fp8
 write_kv_scaled = _ext.write_kv_scaled
 append_kv = _ext.append_kv
 write_kv_batch = _ext.write_kv_batch
+decode_layer_step = _ext.decode_layer_step
 
 __all__ = ["paged_attention", "paged_attention_v2", "paged_attention_v3",
            "paged_attention_v3_lse", "choose_num_splits", "paged_attention_prefill",
            "paged_attention_prefill_wmma", "paged_attention_prefill_simt", "write_kv",
            "validate_block_tables", "merge_states", "paged_attention_v3_fp8",
-           "write_kv_scaled", "append_kv", "write_kv_batch", "shim_path"]
+           "write_kv_scaled", "append_kv", "write_kv_batch", "decode_layer_step", "shim_path"]
 
 
 def shim_path() -> Path:

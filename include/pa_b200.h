@@ -413,6 +413,30 @@ PA_API int pa_append_kv(void* const* k_layers, void* const* v_layers, int pool_d
                         int64_t num_blocks, const float* k_scales, const float* v_scales,
                         int32_t* dev_status, void* stream);
 
+/* One layer of a serving loop's decode step, an addition (the reference's
+ * decode takes fp32 q and returns fp32 out, kernels/paged_attn_v3.cu:211-214,
+ * and writes K/V only through write_kv): pa_paged_attention_v3 with
+ *   - q [num_seqs, num_heads, head_dim] and out (same shape) of io_dtype
+ *     (PA_DTYPE_F32, PA_DTYPE_F16 or PA_DTYPE_BF16; out is rounded to nearest
+ *     even; lse, when given, stays fp32 [num_seqs, num_heads]);
+ *   - when k_new / v_new are given (device [num_seqs, num_kv_heads, head_dim]
+ *     of io_dtype, both or neither), sequence b's new K / V row stored at
+ *     position context_lens[b] - 1 of its pages (converted as pa_write_kv
+ *     does) inside the same launch, before the attention reads it: the
+ *     append and the decode are one kernel.  context_lens counts the new
+ *     token; sequences with context_lens[b] == 0 append nothing.
+ * FP8 pools with k_new return PA_ERR_DTYPE (use pa_append_kv, which takes the
+ * scales).  Workspace: pa_decode_workspace_size for the same shape. */
+PA_API int pa_decode_layer_step(void* out, float* lse, const void* q, int io_dtype,
+                                void* k_cache, void* v_cache, int kv_dtype,
+                                const void* k_new, const void* v_new,
+                                const int32_t* block_tables, const int32_t* context_lens,
+                                int64_t num_seqs, int64_t num_heads, int64_t num_kv_heads,
+                                int64_t head_dim, int64_t block_size, int64_t num_blocks,
+                                int64_t max_blocks, double scale, int64_t num_splits,
+                                void* workspace, size_t workspace_bytes, int32_t* dev_status,
+                                void* stream);
+
 /* Opt-in check of a block table (the reference has none): counts entries
  * used by context_lens that fall outside [0, num_blocks), and sequences whose
  * context exceeds max_blocks * block_size.  Writes the two counts to the

@@ -160,6 +160,20 @@ def test_write_kv_batch_argument_checks():
                      seqs, 2, *args) == 0
 
 
+def test_decode_layer_step_argument_checks():
+    one = ctypes.c_void_p(16)
+    args = (1, 8, 2, 64, 16, 8, 4, 0.125, 0, None, 0, None, None)
+    # q / out in a type the step does not take
+    assert _lib.call("pa_decode_layer_step", one, None, one, _lib.PA_DTYPE_F64, one, one,
+                     _lib.PA_DTYPE_F16, None, None, one, one, *args) == _lib.PA_ERR_DTYPE
+    # a new K row without its V row
+    assert _lib.call("pa_decode_layer_step", one, None, one, _lib.PA_DTYPE_BF16, one, one,
+                     _lib.PA_DTYPE_F16, one, None, one, one, *args) == _lib.PA_ERR_INVALID_ARGUMENT
+    # an FP8 pool cannot take the append (its scales are not arguments here)
+    assert _lib.call("pa_decode_layer_step", one, None, one, _lib.PA_DTYPE_BF16, one, one,
+                     _lib.PA_DTYPE_E4M3, one, one, one, one, *args) == _lib.PA_ERR_DTYPE
+
+
 def test_torch_shim_imports_on_cpu():
     from pa_b200 import ops
     assert ops.shim_path().exists()
