@@ -15,19 +15,19 @@
 
 namespace pa {
 
-const void* decode_kernel_ptr_f16(int D, int QC);
-const void* decode_kernel_ptr_bf16(int D, int QC);
-const void* decode_kernel_ptr_f32(int D, int QC);
-const void* decode_kernel_ptr_f64(int D, int QC);
-const void* decode_kernel_ptr_e4m3(int D, int QC);
+const void* decode_kernel_ptr_f16(int D, int QC, bool step);
+const void* decode_kernel_ptr_bf16(int D, int QC, bool step);
+const void* decode_kernel_ptr_f32(int D, int QC, bool step);
+const void* decode_kernel_ptr_f64(int D, int QC, bool step);
+const void* decode_kernel_ptr_e4m3(int D, int QC, bool step);
 
-const void* decode_kernel_ptr(int dtype, int D, int QC) {
+const void* decode_kernel_ptr(int dtype, int D, int QC, bool step) {
   switch (dtype) {
-    case PA_DTYPE_F16: return decode_kernel_ptr_f16(D, QC);
-    case PA_DTYPE_BF16: return decode_kernel_ptr_bf16(D, QC);
-    case PA_DTYPE_F32: return decode_kernel_ptr_f32(D, QC);
-    case PA_DTYPE_F64: return decode_kernel_ptr_f64(D, QC);
-    case PA_DTYPE_E4M3: return decode_kernel_ptr_e4m3(D, QC);
+    case PA_DTYPE_F16: return decode_kernel_ptr_f16(D, QC, step);
+    case PA_DTYPE_BF16: return decode_kernel_ptr_bf16(D, QC, step);
+    case PA_DTYPE_F32: return decode_kernel_ptr_f32(D, QC, step);
+    case PA_DTYPE_F64: return decode_kernel_ptr_f64(D, QC, step);
+    case PA_DTYPE_E4M3: return decode_kernel_ptr_e4m3(D, QC, step);
     default: return nullptr;
   }
 }
@@ -308,7 +308,9 @@ static int configure(const DecodeArgs& a, Config* c) {
     c->threads = kind == 2 ? 384 : (kind == 1 ? 640 : (c->NS + 1) * 32);
   }
   c->smem = (size_t)c->nstage * stage_bytes + (size_t)c->nstage * (16 + sizeof(StageHeader));
-  c->kernel = decode_kernel_ptr(a.dtype, (int)a.D, QC);
+  // the decode-step instantiation only when the call needs it
+  const bool step = a.io_dtype != PA_DTYPE_F32 || a.k_new != nullptr;
+  c->kernel = decode_kernel_ptr(a.dtype, (int)a.D, QC, step);
   if (!c->kernel) return PA_ERR_HEAD_DIM;
 
   const int64_t rows = a.B * a.qlen;

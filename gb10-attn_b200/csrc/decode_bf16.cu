@@ -3,5 +3,7 @@
 #include "decode_impl.cuh"
 
 namespace pa {
-const void* decode_kernel_ptr_bf16(int D, int QC) { return decode::pick_kernel<__nv_bfloat16>(D, QC); }
+const void* decode_kernel_ptr_bf16(int D, int QC, bool step) {
+  return step ? decode::pick_kernel<__nv_bfloat16, true>(D, QC) : decode::pick_kernel<__nv_bfloat16, false>(D, QC);
+}
 }  // namespace pa

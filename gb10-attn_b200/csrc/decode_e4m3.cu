@@ -3,5 +3,7 @@
 #include "decode_impl.cuh"
 
 namespace pa {
-const void* decode_kernel_ptr_e4m3(int D, int QC) { return decode::pick_kernel<__nv_fp8_e4m3>(D, QC); }
+const void* decode_kernel_ptr_e4m3(int D, int QC, bool step) {
+  return step ? decode::pick_kernel<__nv_fp8_e4m3, true>(D, QC) : decode::pick_kernel<__nv_fp8_e4m3, false>(D, QC);
+}
 }  // namespace pa

@@ -3,5 +3,7 @@
 #include "decode_impl.cuh"
 
 namespace pa {
-const void* decode_kernel_ptr_f16(int D, int QC) { return decode::pick_kernel<__half>(D, QC); }
+const void* decode_kernel_ptr_f16(int D, int QC, bool step) {
+  return step ? decode::pick_kernel<__half, true>(D, QC) : decode::pick_kernel<__half, false>(D, QC);
+}
 }  // namespace pa

@@ -3,5 +3,7 @@
 #include "decode_impl.cuh"
 
 namespace pa {
-const void* decode_kernel_ptr_f32(int D, int QC) { return decode::pick_kernel<float>(D, QC); }
+const void* decode_kernel_ptr_f32(int D, int QC, bool step) {
+  return step ? decode::pick_kernel<float, true>(D, QC) : decode::pick_kernel<float, false>(D, QC);
+}
 }  // namespace pa

@@ -161,6 +161,7 @@ template <> __device__ __forceinline__ __nv_fp8_e4m3 pool_from_f32<__nv_fp8_e4m3
   return r;
 }
 
+
 struct __align__(16) StageHeader {
   int32_t b, gc, tok0, nvalid;
   int32_t flags, seq_k, pad1, pad2;  // seq_k: ordinal among the non-empty sequences
@@ -248,7 +249,7 @@ __device__ __forceinline__ int epoch_arrive(unsigned long long* counter, unsigne
 // keys, clamped to the block table).  CTA b % gridDim fills the output rows of
 // empty sequences (the reference's v3 yields NaN there, paged_attn_v3.cu:160-165).
 template <int D, int TT>
-__device__ __forceinline__ void fused_plan(const Params& p, int32_t* tile_off_s, int32_t* ntok_s,
+__device__ __forceinline__ void fused_plan(const Params& p, int io, int32_t* tile_off_s, int32_t* ntok_s,
                                            int32_t* ne_s, long long* scratch) {
   // one scan carries both counts: tiles in the high bits, non-empty rows in
   // the low 16 (rows <= kFusedRows < 2^16)
@@ -270,7 +271,7 @@ __device__ __forceinline__ void fused_plan(const Params& p, int32_t* tile_off_s,
       if (n <= 0) {
         n = 0;
         if (b % gridDim.x == blockIdx.x) {
-          for (int64_t i = 0; i < p.H * D; ++i) io_store(p.io_dtype, p.out, b * p.H * D + i, p.empty_fill);
+          for (int64_t i = 0; i < p.H * D; ++i) io_store(io, p.out, b * p.H * D + i, p.empty_fill);
           if (p.lse)
             for (int64_t h = 0; h < p.H; ++h) p.lse[b * p.H + h] = -INFINITY;
         }
@@ -395,9 +396,12 @@ __device__ __forceinline__ void merge_pieces_wide(PtrFn ptr, int64_t c0, int64_t
   }
 }
 
-template <typename T, int D, int QC>
+// STEP: the decode-step instantiation (q / out of p.io_dtype, the K / V
+// append); the plain one reads fp32 q and writes fp32 out with no branch.
+template <typename T, int D, int QC, bool STEP>
 __global__ void __launch_bounds__(Limits<T, D, QC>::THREADS, 1)
     decode_kernel(const __grid_constant__ Params p) {
+  const int io = STEP ? p.io_dtype : (int)PA_DTYPE_F32;
   constexpr int TT = Tile<T, QC>::TT;
   using G_ = Geo<T, D, TT>;
   constexpr int VEC = G_::VEC, R = G_::R, NCH = G_::NCH, EPL = G_::EPL;
@@ -440,7 +444,7 @@ __global__ void __launch_bounds__(Limits<T, D, QC>::THREADS, 1)
     int32_t* to_s = reinterpret_cast<int32_t*>(plan_base + kPlanScratchBytes);
     int32_t* nt_s = to_s + p.B + 1;
     int32_t* nz_s = nt_s + p.B;
-    fused_plan<D, TT>(p, to_s, nt_s, nz_s, reinterpret_cast<long long*>(plan_base));
+    fused_plan<D, TT>(p, io, to_s, nt_s, nz_s, reinterpret_cast<long long*>(plan_base));
     tile_off = to_s;
     ntok_s = nt_s;
     ne_s = nz_s;
@@ -559,7 +563,7 @@ __global__ void __launch_bounds__(Limits<T, D, QC>::THREADS, 1)
       int nx_b = 0, nx_gc = 0;           // the next sequence of this CTA's range
       int32_t nx_cur = 0, nx_next = 0;   // its first block-table window
       const int64_t gbytes = (int64_t)p.G * D * (int64_t)sizeof(T);
-      const int64_t qes = p.io_dtype == PA_DTYPE_F32 ? 4 : 2;  // bytes per q element
+      const int64_t qes = io == PA_DTYPE_F32 ? 4 : 2;  // bytes per q element
       const uint32_t qbytes = (uint32_t)(p.G * p.QPK * D * qes);
 
       while (gt < hi) {
@@ -627,7 +631,7 @@ __global__ void __launch_bounds__(Limits<T, D, QC>::THREADS, 1)
         // Decode step with append: the sequence's new K / V row (this g-chunk's
         // heads) goes to position context_lens[b] - 1, the last row of this
         // tile, before the tile is copied; only this CTA reads that row.
-        if (p.k_new != nullptr && r + 1 == s1) {
+        if (STEP && p.k_new != nullptr && r + 1 == s1) {
           const int64_t cb = p.context_lens[b];
           if (cb > 0 && cb <= max_ctx) {
             const int64_t pos = cb - 1;
@@ -642,8 +646,8 @@ __global__ void __launch_bounds__(Limits<T, D, QC>::THREADS, 1)
               T* vd = reinterpret_cast<T*>(const_cast<char*>(p.v_cache) + roff);
               const int64_t src0 = ((int64_t)b * p.HKV + (int64_t)gc * p.G) * D;
               for (int64_t e = lane; e < (int64_t)p.G * D; e += 32) {
-                kd[e] = pool_from_f32<T>(io_load(p.io_dtype, p.k_new, src0 + e));
-                vd[e] = pool_from_f32<T>(io_load(p.io_dtype, p.v_new, src0 + e));
+                kd[e] = pool_from_f32<T>(io_load(io, p.k_new, src0 + e));
+                vd[e] = pool_from_f32<T>(io_load(io, p.v_new, src0 + e));
               }
               // the generic-proxy stores before the bulk copies that read them
               asm volatile("fence.proxy.async.global;" ::: "memory");
@@ -777,7 +781,7 @@ __global__ void __launch_bounds__(Limits<T, D, QC>::THREADS, 1)
       for (int k = 0; k < PERG; ++k) {
         const int j = (32 * k) / D;
         const int e = (lane + 32 * k) - j * D;
-        io_store(p.io_dtype, p.out, ((int64_t)pb * p.H + phead0 + j) * D + e, __int_as_float(0x7fc00000));
+        io_store(io, p.out, ((int64_t)pb * p.H + phead0 + j) * D + e, __int_as_float(0x7fc00000));
       }
       if (p.lse && lane < QC) p.lse[(int64_t)pb * p.H + phead0 + lane] = __int_as_float(0x7fc00000);
       if (lane == 0) report(p.dev_status, PA_DEVERR_MERGE);
@@ -827,7 +831,7 @@ __global__ void __launch_bounds__(Limits<T, D, QC>::THREADS, 1)
       for (int k = 0; k < PER; ++k) {
         const int j = (32 * k) / D;
         const int e = (lane + 32 * k) - j * D;
-        io_store(p.io_dtype, p.out, ((int64_t)pb * p.H + phead0 + j) * D + e, o[k] / lg[j]);
+        io_store(io, p.out, ((int64_t)pb * p.H + phead0 + j) * D + e, o[k] / lg[j]);
       }
       if (p.lse && lane < QC) {
 #pragma unroll
@@ -879,7 +883,7 @@ __global__ void __launch_bounds__(Limits<T, D, QC>::THREADS, 1)
           const int64_t src = q0 + (int64_t)j * D + (c * R + li) * VEC;
 #pragma unroll
           for (int v = 0; v < VEC; v += 2) {
-            const float2 x = io_load2(p.io_dtype, p.q, src + v);
+            const float2 x = io_load2(io, p.q, src + v);
             qf[j][c * VEC + v] = x.x * qs;
             qf[j][c * VEC + v + 1] = x.y * qs;
           }
@@ -1031,7 +1035,7 @@ __global__ void __launch_bounds__(Limits<T, D, QC>::THREADS, 1)
               float2 y;
               y.x = acc[j][c * VEC + v] * inv;
               y.y = acc[j][c * VEC + v + 1] * inv;
-              io_store2(p.io_dtype, p.out, o + (c * R + li) * VEC + v, y);
+              io_store2(io, p.out, o + (c * R + li) * VEC + v, y);
             }
           }
           if (p.lse && li == 0) p.lse[(int64_t)b * p.H + head0 + j] = (m[j] + __log2f(l[j])) * kLn2;
@@ -1078,7 +1082,7 @@ __global__ void __launch_bounds__(Limits<T, D, QC>::THREADS, 1)
 }  // namespace decode
 
 // Kernel pointer for an instantiation (nullptr if not instantiated).
-const void* decode_kernel_ptr(int dtype, int D, int QC);
+const void* decode_kernel_ptr(int dtype, int D, int QC, bool step);
 int decode_max_warps(int dtype, int D, int QC);
 int decode_elems_per_lane(int dtype, int D);
 
@@ -1087,33 +1091,33 @@ int decode_elems_per_lane(int dtype, int D);
 namespace pa {
 namespace decode {
 
-template <typename T, int D, int QC>
+template <typename T, int D, int QC, bool STEP>
 const void* kernel_if_fits() {
   if constexpr (QC * Geo<T, D>::EPL <= (sizeof(T) <= 2 ? 64 : (sizeof(T) == 4 ? 32 : 16))) {
-    return reinterpret_cast<const void*>(&decode_kernel<T, D, QC>);
+    return reinterpret_cast<const void*>(&decode_kernel<T, D, QC, STEP>);
   } else {
     return nullptr;
   }
 }
 
-template <typename T, int D>
+template <typename T, int D, bool STEP>
 const void* pick_qc(int QC) {
   switch (QC) {
-    case 1: return kernel_if_fits<T, D, 1>();
-    case 2: return kernel_if_fits<T, D, 2>();
-    case 4: return kernel_if_fits<T, D, 4>();
-    case 8: return kernel_if_fits<T, D, 8>();
+    case 1: return kernel_if_fits<T, D, 1, STEP>();
+    case 2: return kernel_if_fits<T, D, 2, STEP>();
+    case 4: return kernel_if_fits<T, D, 4, STEP>();
+    case 8: return kernel_if_fits<T, D, 8, STEP>();
     default: return nullptr;
   }
 }
 
-template <typename T>
+template <typename T, bool STEP>
 const void* pick_kernel(int D, int QC) {
   switch (D) {
-    case 32: return pick_qc<T, 32>(QC);
-    case 64: return pick_qc<T, 64>(QC);
-    case 128: return pick_qc<T, 128>(QC);
-    case 256: return pick_qc<T, 256>(QC);
+    case 32: return pick_qc<T, 32, STEP>(QC);
+    case 64: return pick_qc<T, 64, STEP>(QC);
+    case 128: return pick_qc<T, 128, STEP>(QC);
+    case 256: return pick_qc<T, 256, STEP>(QC);
     default: return nullptr;
   }
 }
