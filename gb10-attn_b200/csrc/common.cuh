@@ -206,6 +206,40 @@ __device__ __forceinline__ bool mbar_try_wait_cl(uint64_t* bar, uint32_t parity,
   return ok != 0;
 }
 
+// try_wait with relaxed semantics at cluster scope: for barriers that only
+// hand tensor-memory data between threads and the tensor core (an MMA's
+// commit, or threads' tcgen05.st + tcgen05.wait::st); the tcgen05 fences on
+// both sides order that data, and an acquire at cluster scope would add
+// nothing but its cost.
+__device__ __forceinline__ bool mbar_try_wait_rx(uint64_t* bar, uint32_t parity, uint32_t hint_ns) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.relaxed.cluster.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity), "r"(hint_ns)
+      : "memory");
+  return ok != 0;
+}
+
+// The bounded wait on such a barrier.
+__device__ __forceinline__ bool mbar_wait_rx(uint64_t* bar, uint32_t parity, int32_t* abort_flag,
+                                             int32_t abort_tag = 1) {
+  if (mbar_try_wait_rx(bar, parity, 0u)) return true;
+  const uint64_t t0 = globaltimer_ns();
+  for (uint32_t it = 1;; ++it) {
+    if (mbar_try_wait_rx(bar, parity, 100000u)) return true;
+    if ((it & 7) == 0) {
+      if (abort_flag && *reinterpret_cast<volatile int32_t*>(abort_flag) == abort_tag) return false;
+      if (globaltimer_ns() - t0 > kWaitLimitNs) {
+        if (abort_flag) atomicExch(abort_flag, abort_tag);
+        return false;
+      }
+    }
+  }
+}
+
 __device__ __forceinline__ bool mbar_wait_cl(uint64_t* bar, uint32_t parity, int32_t* abort_flag,
                                              int32_t abort_tag = 1) {
   if (mbar_try_wait_cl(bar, parity, 0u)) return true;

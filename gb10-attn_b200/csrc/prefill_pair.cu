@@ -198,7 +198,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       for (int j = 0; j < n_tiles && ok; ++j) {
         for (int k = 0; k < 2 && ok; ++k) {
           if (j >= ntile[k]) continue;
-          if (!mbar_wait_cl(&p_full[k], j & 1, abort_s)) { ok = false; break; }
+          if (!mbar_wait_rx(&p_full[k], j & 1, abort_s)) { ok = false; break; }
           const int vs = j % NV;
           if (j > v_seen) {
             if (!mbar_wait_cl(&v_full[vs], (j / NV) & 1, abort_s)) { ok = false; break; }

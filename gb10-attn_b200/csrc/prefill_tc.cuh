@@ -191,6 +191,16 @@ __device__ __forceinline__ bool warp_wait_t(uint64_t* bar, uint32_t parity, int3
   return ok != 0;
 }
 
+// Warp-uniform bounded wait on a barrier that hands tensor-memory data on
+// (mbar_wait_rx: relaxed, cluster scope).
+__device__ __forceinline__ bool warp_wait_rx(uint64_t* bar, uint32_t parity, int32_t* abort_flag) {
+  int ok = 1;
+  if ((threadIdx.x & 31) == 0) ok = mbar_wait_rx(bar, parity, abort_flag) ? 1 : 0;
+  ok = __shfl_sync(0xffffffffu, ok, 0);
+  if (ok) (void)mbar_wait_rx(bar, parity, abort_flag);
+  return ok != 0;
+}
+
 // Arrival on a barrier the MMA issuer waits on: this CTA's own, or in a CTA
 // pair the leader's (even CTA) through its cluster address, with release at
 // cluster scope.
@@ -462,7 +472,7 @@ __device__ __forceinline__ void softmax_chain(const Params& p, unsigned char* sm
   float m_ref = -INFINITY, l = 0.f;
   bool ok = true;
   for (int j = 0; j < n_tiles && ok; ++j) {
-    if (!warp_wait_t<true>(&s_full[grp], j & 1, abort_s)) { ok = false; break; }
+    if (!warp_wait_rx(&s_full[grp], j & 1, abort_s)) { ok = false; break; }
     tc::fence_after_sync();
     // causal rule + context bound (kernels/paged_attn_prefill.cu:62-65):
     // keys k0 + c of this tile are visible when c < lim
@@ -525,7 +535,7 @@ __device__ __forceinline__ void softmax_chain(const Params& p, unsigned char* sm
     l += ls.x + ls.y;
     if (rescale) {
       // the chain's previous P V must have finished
-      if (!warp_wait_t<true>(&o_ready[grp], (j - 1) & 1, abort_s)) { ok = false; break; }
+      if (!warp_wait_rx(&o_ready[grp], (j - 1) & 1, abort_s)) { ok = false; break; }
       tc::fence_after_sync();
 #pragma unroll
       for (int c4 = 0; c4 < D / 32; ++c4) {
@@ -537,15 +547,19 @@ __device__ __forceinline__ void softmax_chain(const Params& p, unsigned char* sm
         tc::tmem_st32(lane_base + ocol + 32 * c4, o);
       }
     }
-    // every lane's P (and O) stores complete, then one arrival per warp
+    // every lane's P (and O) stores complete, then one arrival per warp, to
+    // the leader's barrier, relaxed: P is tensor-memory data, ordered by
+    // tcgen05.wait::st and the fence; no generic write needs releasing (a
+    // release at cluster scope here cost ~1-2 thousand cycles per tile and
+    // lay on the chain's critical path)
     tc::tmem_wait_st();
     tc::fence_before_sync();
     __syncwarp();
-    if (lane == 0) arrive_to_leader<true>(&p_full[grp]);
+    if (lane == 0) tc::mbar_arrive_cluster_relaxed(tc::mapa_shared(&p_full[grp], 0));
   }
 
   // epilogue: O / l -> out, 32 columns at a time
-  if (ok && n_tiles > 0 && !warp_wait_t<true>(&o_ready[grp], (n_tiles - 1) & 1, abort_s)) ok = false;
+  if (ok && n_tiles > 0 && !warp_wait_rx(&o_ready[grp], (n_tiles - 1) & 1, abort_s)) ok = false;
   const bool have = ok && n_tiles > 0;
   const float inv = l > 0.f ? 1.f / l : 0.f;
   if (have) tc::fence_after_sync();

@@ -220,6 +220,16 @@ __device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
                : "memory");
 }
 
+// The same arrival with relaxed semantics: for a barrier that only hands
+// tensor-memory data on (this thread's tcgen05.st completed by
+// tcgen05.wait::st, then tcgen05.fence::before_thread_sync); a release at
+// cluster scope costs ~1-2 thousand cycles per arrival and orders nothing
+// that such a handoff needs.
+__device__ __forceinline__ void mbar_arrive_cluster_relaxed(uint32_t cluster_addr) {
+  asm volatile("mbarrier.arrive.relaxed.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr)
+               : "memory");
+}
+
 // All threads of both CTAs: every thread's earlier writes (shared memory
 // included) are visible cluster-wide after it.
 __device__ __forceinline__ void cluster_sync() {
