@@ -108,3 +108,35 @@ def test_tensor_core_path_pages_in_order(dtype, D, BS):
     scale = D ** -0.5
     out = abi_prefill(q, k, v, bt, ctx, scale, dtype)
     assert max_abs(out, orc.prefill(q, k, v, bt, ctx, scale, threads=8)) <= 2e-3
+
+
+@pytest.mark.parametrize("dtype", ["bfloat16", "float16"])
+def test_pair_path_repeats_bit_for_bit(dtype):
+    # The CTA pairs hand S, P and O between the softmax warps and the tensor
+    # core through barriers with relaxed semantics (the tcgen05 fences order
+    # that tensor-memory data).  A missing order would show up as results
+    # that change from launch to launch: 20 launches over 3 x 8 heads x 2
+    # items of 512 rows must give identical bits, and the first must match
+    # the oracle.
+    q, k, v, bt, ctx = case(48, 3, 1000, 8, 4, 128, 16, [1000, 1200, 1500], dtype)
+    scale = 128 ** -0.5
+    kd, vd = to_dev(k, dtype), to_dev(v, dtype)
+    first = abi_prefill(q, kd, vd, bt, ctx, scale, dtype)
+    assert max_abs(first, orc.prefill(q, k, v, bt, ctx, scale, threads=8)) <= 2e-3
+    for _ in range(19):
+        again = abi_prefill(q, kd, vd, bt, ctx, scale, dtype)
+        assert np.array_equal(again.view(np.uint32), first.view(np.uint32))
+
+
+@pytest.mark.parametrize("dtype", ["bfloat16", "float16"])
+def test_pair_path_ragged_items_and_empty_chains(dtype):
+    # head_dim 128 on CTA pairs, 512 query rows per pair as two chains of 256:
+    # 3 x 40 heads x 2 items = 240 items.  Sq = 600: the second item's second
+    # chain (rows 768..) is empty; ctx 100 < Sq leaves the first item's first
+    # chain with no visible key while its second chain has one tile; ctx 900
+    # puts a cached prefix before the chunk.
+    q, k, v, bt, ctx = case(47, 3, 600, 40, 8, 128, 16, [900, 600, 100], dtype)
+    scale = 128 ** -0.5
+    out = abi_prefill(q, k, v, bt, ctx, scale, dtype)
+    assert np.all(out[2, :500] == 0)
+    assert max_abs(out, orc.prefill(q, k, v, bt, ctx, scale, threads=8)) <= 2e-3
